@@ -1,0 +1,355 @@
+#!/usr/bin/env python3
+"""Headline benchmark: device copy bandwidth of a 4 GiB buffer on B200.
+
+Workload (the north-star configuration that fits one GPU): src and dst are
+4 GiB contiguous uint8 buffers of seeded random bytes; one step is one copy
+through libtcb's copy kernel; dst must equal src bit-exactly.  Bandwidth
+counts read + write traffic, 2 x 4 GiB per step, in decimal GB/s.  The
+buffers are 34x the 126 MB L2, so no cache flush is needed between steps.
+
+`python bench.py --gpus N --steps K --warmup W` runs N independent replicas
+(one process per GPU under torchrun, no collective on the data path; host
+coordination over gloo), times exactly K steps with CUDA events between
+barriers, takes the max over ranks and prints one JSON line on rank 0.
+`--impl reference` times the reference's CPU path for the same workload
+(a host copy of the buffer, restated in oracle/tcb_oracle.c) on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import statistics
+import sys
+import threading
+import time
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+BUFFER_BYTES = 4 * 2**30
+METRIC = "memory_bandwidth (device copy, read+write bytes)"
+UNIT = "GB/s"
+WORKLOAD = "device copy of a 4 GiB uint8 buffer (src -> dst), seeded random bytes, bit-exact"
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="ldg128")
+    parser.add_argument("--threads", type=int, default=512)
+    parser.add_argument("--blocks", type=int, default=0, help="CTAs (0: library default)")
+    parser.add_argument("--e2e-steps", type=int, default=3,
+                        help="steps of the host-buffer end-to-end leg")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0,
+                        help="CPU-baseline sample duration")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args()
+
+
+# ---------------------------------------------------------------- plumbing
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_group(world: int):
+    if world <= 1:
+        return None
+    import datetime
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def all_max(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def all_sum(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML (read-only)."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap", 0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown", 0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown", 0x0000000000000002: "applications_clocks_setting",
+        0x0000000000000100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[device_index]) if visible else device_index
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+            self.error = str(exc)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0, "source": "nvml"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
+
+
+# --------------------------------------------------------------- baselines
+def measured_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+def ncu_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = REPO / "profiles" / "ncu_traffic.json"
+    if not path.exists():
+        return None
+    table = json.loads(path.read_text())
+    entry = table.get(kernel)
+    return None if entry is None else float(entry["dram_bytes_per_launch"])
+
+
+def cpu_copy_baseline(seconds: float, sample_bytes: int = BUFFER_BYTES) -> dict:
+    """Host copy of the workload (oracle restatement), all host threads."""
+    import numpy as np
+
+    from oracle import native
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    src = rng.integers(0, 256, size=sample_bytes, dtype=np.uint8)
+    dst = np.empty_like(src)
+    native.copy(src, dst, threads)  # first touch
+    copies, start = 0, time.perf_counter()
+    used = threads
+    while True:
+        used = native.copy(src, dst, threads)
+        copies += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            break
+    if not np.array_equal(src[:1 << 20], dst[:1 << 20]):
+        raise AssertionError("host copy mismatch")
+    value = 2 * sample_bytes * copies / elapsed / 1e9
+    return {"value": value, "unit": UNIT, "cores": used, "kind": "port",
+            "sample": f"{copies} host copies of a {sample_bytes / 2**30:g} GiB uint8 buffer "
+                      f"({elapsed:.1f} s, {used} threads, oracle/tcb_oracle.c oracle_copy)"}
+
+
+# --------------------------------------------------------------- our impl
+def run_ours(args):
+    import torch
+
+    from triton_chip_benchmarks_b200 import _native
+
+    world, rank, local = dist_env()
+    dist = init_group(world)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    variant = {"ldg128": _native.COPY_LDG128, "bulk": _native.COPY_BULK}[args.variant]
+    threads = args.threads if args.variant == "ldg128" else 32
+
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    src = torch.randint(0, 256, (BUFFER_BYTES,), dtype=torch.uint8, device=device, generator=gen)
+    dst = torch.zeros_like(src)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        _native.copy(src, dst, BUFFER_BYTES, variant, args.blocks, threads, stream)
+
+    step()
+    torch.cuda.synchronize()
+    if not torch.equal(src, dst):
+        raise AssertionError("copy validation failed: dst != src")
+    dst.zero_()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if not torch.equal(src, dst):
+        raise AssertionError("copy validation failed after warmup")
+
+    sampler = ClockSampler(local)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    torch.cuda.synchronize()
+    sampler.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier(dist)
+    local_ms = start.elapsed_time(end)
+    ms = all_max(dist, local_ms)
+    ms_per_step = ms / args.steps
+    traffic = 2 * BUFFER_BYTES
+    value = world * traffic * args.steps / (ms / 1e3) / 1e9
+
+    # End to end through the C ABI with host buffers: H2D of the step's input
+    # from pinned memory, the copy kernel, D2H of the result, all timed.
+    host_src = src.cpu().pin_memory()
+    host_dst = torch.empty_like(host_src).pin_memory()
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    torch.cuda.synchronize()
+    e2e_start.record(stream)
+    for _ in range(args.e2e_steps):
+        src.copy_(host_src, non_blocking=True)
+        step()
+        host_dst.copy_(dst, non_blocking=True)
+    e2e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    e2e_ms = all_max(dist, e2e_start.elapsed_time(e2e_end))
+    if not torch.equal(host_src[: 1 << 24], host_dst[: 1 << 24]):
+        raise AssertionError("end-to-end copy mismatch")
+    e2e_value = world * traffic * args.e2e_steps / (e2e_ms / 1e3) / 1e9
+    del host_src, host_dst
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    peak_note = "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    if peak is None:
+        peak, peak_note = 6650.0, "of fallback"
+    kernel_name = f"copy_{args.variant}"
+    achieved = traffic / (local_ms / args.steps / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": ncu_traffic(kernel_name),
+                "peak_source": peak_note, "algorithmic_bytes_per_launch": traffic,
+                "kernel": kernel_name}
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_copy_baseline(args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded random bytes)",
+        "config": {"workload": WORKLOAD, "buffer_bytes": BUFFER_BYTES,
+                   "bytes_per_step": traffic, "kernel": kernel_name,
+                   "threads_per_cta": threads, "ctas": args.blocks or "library default",
+                   "l2": "no flush: inputs (4 GiB) larger than the 126 MB L2",
+                   "parallelism": f"replicas x{world} (no collective)"},
+        "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": BUFFER_BYTES,
+                "d2h_bytes_per_step": BUFFER_BYTES, "steps": args.e2e_steps,
+                "path": "pinned host -> device, tcb_copy, device -> pinned host"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import native
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1234)
+    src = rng.integers(0, 256, size=BUFFER_BYTES, dtype=np.uint8)
+    dst = np.zeros_like(src)
+    for _ in range(args.warmup):
+        native.copy(src, dst, threads)
+    if not np.array_equal(src, dst):
+        raise AssertionError("host copy mismatch")
+    start = time.perf_counter()
+    used = threads
+    for _ in range(args.steps):
+        used = native.copy(src, dst, threads)
+    elapsed = time.perf_counter() - start
+    traffic = 2 * BUFFER_BYTES
+    value = traffic * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded random bytes)",
+        "config": {"workload": WORKLOAD, "buffer_bytes": BUFFER_BYTES, "bytes_per_step": traffic,
+                   "parallelism": "host threads on rank 0"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "port",
+                         "sample": f"full 4 GiB buffer per step, {used} host threads "
+                                   "(oracle/tcb_oracle.c oracle_copy)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

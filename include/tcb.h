@@ -1,0 +1,178 @@
+/*
+ * tcb.h - C ABI of the B200 (sm_100a) chip-peak probe library, libtcb.so.
+ *
+ * The library holds the device hot paths of the chip metric suite: the
+ * resident-operand tensor multiply-add probe, the vector FMA-chain probe and
+ * the device copy/read bandwidth probe.  Each entry point below replaces one
+ * Triton launch wrapper of the reference suite (huangyiqun/triton_chip_benchmarks);
+ * the replaced function is named beside it as file:line.
+ *
+ * Conventions for every launch entry point:
+ *   - Pointers are device pointers owned by the caller.  The library never
+ *     allocates or frees device memory and never synchronizes the device on a
+ *     launch path, so a launch can be captured into a CUDA graph.
+ *   - `stream` is a cudaStream_t (for PyTorch: torch.cuda.current_stream().cuda_stream).
+ *   - The return value is TCB_OK (0) or a negative TCB_ERR_* code.  Argument,
+ *     capability and resource problems are detected on the host before any
+ *     launch.  Device-side waits are bounded; a wait that runs out writes
+ *     TCB_ERR_TIMEOUT into `status_dev` (an int32 device word, may be NULL)
+ *     and the kernel returns.
+ *   - One host thread per process drives one device (the current device).
+ */
+#ifndef TCB_H_
+#define TCB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *tcb_stream_t; /* identical to cudaStream_t */
+
+/* ---------------------------------------------------------------- status */
+#define TCB_OK 0
+#define TCB_ERR_INVALID_ARGUMENT (-1) /* bad pointer, size, shape or flag */
+#define TCB_ERR_UNSUPPORTED (-2)      /* capability: format/tile not provided on this device */
+#define TCB_ERR_RESOURCE (-3)         /* configuration exceeds shared/tensor memory or registers */
+#define TCB_ERR_LAUNCH (-4)           /* the CUDA launch itself failed */
+#define TCB_ERR_DEVICE (-5)           /* a device query failed */
+#define TCB_ERR_TIMEOUT (-6)          /* device-side bounded wait ran out (status word only) */
+#define TCB_ERR_ALIGNMENT (-7)        /* pointer or size not aligned as the kernel requires */
+
+/* Human-readable text for a status code (static storage). */
+const char *tcb_strerror(int status);
+/* Library version and build target, e.g. "tcb 0.1.0 sm_100a". */
+const char *tcb_version(void);
+
+/* ------------------------------------------------------------- device */
+typedef struct tcb_device_props {
+  char name[256];
+  int major, minor;          /* compute capability */
+  int sm_count;              /* streaming multiprocessors */
+  int max_smem_per_block;    /* opt-in dynamic shared memory per CTA, bytes */
+  int max_smem_per_sm;       /* shared memory per SM, bytes */
+  int regs_per_sm;           /* 32-bit registers per SM */
+  int clock_khz;             /* max SM clock */
+  int mem_clock_khz;         /* max memory clock */
+  int mem_bus_width;         /* bits */
+  long long l2_cache_bytes;  /* L2 capacity */
+  long long total_mem_bytes; /* device memory capacity */
+  long long free_mem_bytes;  /* currently free device memory */
+  int driver_version, runtime_version;
+} tcb_device_props;
+
+/* Properties of `device`.  Replaces the property probing of setup_device
+ * (common.py:214-292) and the capacity probe of probe_device
+ * (bench_suite.py:106-114). */
+int tcb_device_query(int device, tcb_device_props *out);
+
+/* --------------------------------------------------------- copy / read */
+#define TCB_COPY_LDG128 0 /* persistent grid-stride 128-bit loads/stores */
+#define TCB_COPY_BULK 1   /* bulk-copy engine: global -> shared -> global, one lane per CTA */
+
+/* dst[0:bytes) = src[0:bytes).  blocks = 0 selects 4 x SM count; threads = 0
+ * selects 512.  Any byte count and alignment is accepted; the vector path
+ * needs 16-byte aligned pointers and falls back to a byte loop otherwise.
+ * Replaces launch_copy (bench_bandwidth.py:43-47) and copy_kernel
+ * (bench_bandwidth.py:36-40). */
+int tcb_copy(const void *src, void *dst, size_t bytes, int variant, int blocks, int threads,
+             tcb_stream_t stream);
+
+#define TCB_READ_FP32 0
+#define TCB_READ_FP16 1
+#define TCB_READ_BF16 2
+/* sink[i] = FP32 sum of src[i*block_elems : (i+1)*block_elems) (the last
+ * block may be partial).  block_elems is a power of two in [256, 65536].
+ * Replaces launch_read (bench_bandwidth.py:62-67) and read_kernel
+ * (bench_bandwidth.py:50-59). */
+int tcb_read(const void *src, int dtype, long long elements, float *sink, int block_elems,
+             int threads, tcb_stream_t stream);
+
+/* ------------------------------------------------------ vector chains */
+#define TCB_V_BF16 0       /* fma.rn.bf16x2, packed pairs */
+#define TCB_V_FP16 1       /* fma.rn.f16x2, packed pairs */
+#define TCB_V_FP32 2       /* fma.rn.f32 */
+#define TCB_V_FP64 3       /* fma.rn.f64 */
+#define TCB_V_INT8_DP4A 4  /* dp4a.s32.s32 on int32 words, 8 ops per update */
+#define TCB_V_INT32_IMAD 5 /* mad.lo.s32 (int32 wrap), 2 ops per update */
+#define TCB_V_INT8_MULADD 6 /* int8 state, (x*a + b) mod 256, 2 ops per update */
+
+/* Eight independent chains per element: out[c][e] = f^iterations(in[c][e])
+ * with f(x) = x*coeff[0] + coeff[1+c] (dp4a: f(x) = dot4(x, coeff[0]) + coeff[1+c]).
+ * in/out are [8][elements] in the dtype's storage (int32 words for DP4A and
+ * IMAD, int8 for MULADD), coeff holds 9 values of the same storage type.
+ * elements must equal blocks * threads * elems_per_thread; elems_per_thread
+ * is one of 1,2,4,8,16 (even for the packed 16-bit types); unroll is one of
+ * 1,2,4,8,16 (any iteration count is accepted).  Replaces launch_vector
+ * (bench_vector.py:1032-1051) and vector_fma_kernel (bench_vector.py:182-319). */
+int tcb_vector_chains(int dtype, const void *in, void *out, const void *coeff,
+                      long long elements, int iterations, int blocks, int threads,
+                      int elems_per_thread, int unroll, tcb_stream_t stream);
+
+/* ------------------------------------------------------ tensor probe */
+#define TCB_T_BF16 0
+#define TCB_T_FP16 1
+#define TCB_T_TF32 2      /* fp32 storage, tcgen05 kind::tf32 */
+#define TCB_T_FP32 3      /* IEEE fp32, SIMT FFMA (no IEEE-fp32 tensor instruction exists) */
+#define TCB_T_FP64 4
+#define TCB_T_INT8 5      /* int8 in, int32 accumulate */
+#define TCB_T_FP8E4M3 6   /* e4m3fn in, fp32 accumulate */
+#define TCB_T_MXF4 7      /* OCP MX E2M1 packed two per byte (low nibble = even k), E8M0 scales */
+
+#define TCB_TV_TCGEN05 0  /* tcgen05.mma, accumulators in tensor memory */
+#define TCB_TV_DMMA 1     /* mma.sync f64 (fp64 only) */
+#define TCB_TV_SIMT 2     /* scalar FFMA / DFMA (fp32, fp64) */
+
+/* Resident-operand probe.  CTA b loads A_b and B_{c,b} (c < chains) once and
+ * then accumulates C_{c,b} += A_b . B_{c,b}^T `iterations` times.
+ *   A  : [blocks][tile_m][tile_k]            row-major (K contiguous)
+ *   B  : [chains][blocks][tile_n][tile_k]    K contiguous (i.e. B^T of the [K][N] operand)
+ *   C  : [chains][blocks][tile_m][tile_n]    fp32 (int32 for INT8, fp64 for FP64)
+ *   For MXF4 the K axis is packed (tile_k/2 bytes per row) and
+ *   SA : [blocks][tile_m][tile_k/32], SB : [blocks][tile_n][tile_k/32] E8M0 bytes.
+ * blocks_per_sm is the intended residency (it sizes the tensor-memory share
+ * and shared-memory reservation of each CTA).  Replaces _launch_peak
+ * (bench_tensor.py:581-600) with _tensor_peak_kernel (bench_tensor.py:406-449)
+ * and _tensor_peak_scaled_kernel (bench_tensor.py:452-488). */
+int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const void *SA,
+                    const void *SB, void *C, int blocks, int blocks_per_sm, int tile_m,
+                    int tile_n, int tile_k, int chains, int iterations, int *status_dev,
+                    tcb_stream_t stream);
+
+/* ------------------------------------------------------- kernel info */
+#define TCB_FAMILY_COPY 0
+#define TCB_FAMILY_READ 1
+#define TCB_FAMILY_VECTOR 2
+#define TCB_FAMILY_TENSOR 3
+#define TCB_FAMILY_GEMM_FP4 4
+
+typedef struct tcb_kernel_info_t {
+  int registers_per_thread;  /* cudaFuncAttributes.numRegs */
+  int local_bytes_per_thread; /* cudaFuncAttributes.localSizeBytes (spill indicator) */
+  int static_smem_bytes;
+  int dynamic_smem_bytes;    /* what the launch requests */
+  int max_threads_per_block;
+  int threads_per_block;     /* what the launch uses */
+  int tensor_core;           /* 1: the arithmetic runs on tensor cores */
+  char instruction[128];     /* the arithmetic instruction written in the kernel source */
+  char execution_kind[16];   /* "tensor" or "simt" */
+} tcb_kernel_info_t;
+
+/* Static facts about the kernel a launch with these arguments would run.
+ * `a0..a5` are the family's launch parameters:
+ *   COPY   : variant, threads
+ *   READ   : dtype, threads
+ *   VECTOR : dtype, threads, elems_per_thread, unroll
+ *   TENSOR : dtype, variant, tile_m, tile_n, tile_k, chains (blocks_per_sm via a6)
+ * Replaces the CompiledKernel metadata read by _compiled_info
+ * (bench_tensor.py:984-1146) and inspect_assembly (bench_vector.py:623-799). */
+int tcb_kernel_info(int family, int a0, int a1, int a2, int a3, int a4, int a5, int a6,
+                    tcb_kernel_info_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TCB_H_ */

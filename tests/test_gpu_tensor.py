@@ -1,0 +1,183 @@
+"""Resident tensor-probe kernels through the C ABI against the exact oracle (GPU).
+
+Operands are small integers scaled by powers of two, so every product and
+partial sum is exactly representable: the kernels must match the oracle's
+iterations * (A . B^T) bit for bit.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tensor as oracle_tensor
+
+pytestmark = pytest.mark.gpu
+
+BF16, FP16, TF32, FP32, FP64, INT8, FP8, MXF4 = range(8)
+TCGEN05, DMMA, SIMT = 0, 1, 2
+STORAGE = {BF16: torch.bfloat16, FP16: torch.float16, TF32: torch.float32,
+           FP32: torch.float32, FP64: torch.float64, INT8: torch.int8,
+           FP8: torch.float8_e4m3fn}
+NAME = {BF16: "bf16", FP16: "fp16", TF32: "tf32", FP32: "fp32", FP64: "fp64", INT8: "int8",
+        FP8: "fp8", MXF4: "fp4"}
+
+
+def _operands(dtype, blocks, chains, m, n, k, seed):
+    gen = torch.Generator().manual_seed(seed)
+    if dtype == MXF4:
+        a_codes = torch.randint(0, 16, (blocks, m, k), generator=gen, dtype=torch.uint8)
+        b_codes = torch.randint(0, 16, (chains, blocks, n, k), generator=gen, dtype=torch.uint8)
+        return (torch.from_numpy(oracle_tensor.pack_e2m1_pairs(a_codes.numpy())),
+                torch.from_numpy(oracle_tensor.pack_e2m1_pairs(b_codes.numpy())))
+    ia = torch.randint(-3, 4, (blocks, m, k), generator=gen)
+    ib = torch.randint(-3, 4, (chains, blocks, n, k), generator=gen)
+    if dtype == INT8:
+        return ia.to(torch.int8), ib.to(torch.int8)
+    return (ia.double() / 4).to(STORAGE[dtype]), (ib.double() / 4).to(STORAGE[dtype])
+
+
+def _host(t):
+    if t.dtype == torch.float8_e4m3fn:
+        return t.double().numpy()
+    if t.dtype == torch.bfloat16:
+        return t.double().numpy()
+    return t.numpy()
+
+
+def _run(native, cuda, dtype, variant, a, b, m, n, k, chains, blocks, iterations, bps=1,
+         sa=None, sb=None):
+    out_dtype = torch.int32 if dtype == INT8 else torch.float64 if dtype == FP64 else torch.float32
+    c = torch.full((chains, blocks, m, n), -7, dtype=out_dtype, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    native.tensor_peak(dtype, variant, a.to(cuda), b.to(cuda), c, blocks=blocks,
+                       blocks_per_sm=bps, tile_m=m, tile_n=n, tile_k=k, chains=chains,
+                       iterations=iterations, scale_a=None if sa is None else sa.to(cuda),
+                       scale_b=None if sb is None else sb.to(cuda), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return c.cpu()
+
+
+def _check(dtype, got, a, b, iterations, sa=None, sb=None):
+    chains, blocks = got.shape[0], got.shape[1]
+    av = _host(a)
+    bv = _host(b)
+    for c in range(chains):
+        if dtype == MXF4:
+            ref = oracle_tensor.resident_reference(
+                av, bv[c], iterations, "fp4",
+                None if sa is None else sa.numpy(), None if sb is None else sb.numpy())
+        else:
+            ref = oracle_tensor.resident_reference(av, bv[c], iterations, NAME[dtype])
+        assert np.array_equal(got[c].double().numpy(), ref.astype(np.float64)), \
+            f"chain {c}: max err {np.abs(got[c].double().numpy() - ref).max()}"
+
+
+TC_CASES = [
+    # dtype, m, n, k, chains
+    (BF16, 128, 128, 64, 1), (BF16, 128, 256, 32, 2), (BF16, 256, 256, 64, 1),
+    (FP16, 128, 256, 64, 1), (FP16, 256, 256, 128, 1),
+    (TF32, 128, 128, 32, 2), (TF32, 256, 256, 32, 1),
+    (INT8, 128, 256, 64, 2), (INT8, 256, 256, 128, 1),
+    (FP8, 128, 128, 64, 2), (FP8, 256, 256, 128, 1),
+    (MXF4, 128, 128, 128, 2), (MXF4, 256, 256, 256, 1), (MXF4, 128, 256, 512, 1),
+]
+
+
+@pytest.mark.parametrize("dtype,m,n,k,chains", TC_CASES)
+@pytest.mark.parametrize("iterations", [1, 3, 64])
+def test_tcgen05_exact(cuda, native, dtype, m, n, k, chains, iterations):
+    blocks = 3
+    a, b = _operands(dtype, blocks, chains, m, n, k, seed=m + n + k + iterations)
+    sa = sb = None
+    if dtype == MXF4:
+        sa = torch.full((blocks, m, k // 32), 127, dtype=torch.uint8)
+        sb = torch.full((blocks, n, k // 32), 127, dtype=torch.uint8)
+    got = _run(native, cuda, dtype, TCGEN05, a, b, m, n, k, chains, blocks, iterations,
+               sa=sa, sb=sb)
+    _check(dtype, got, a, b, iterations, sa, sb)
+
+
+@pytest.mark.parametrize("bps", [2, 4])
+def test_tcgen05_blocks_per_sm(cuda, native, bps):
+    m, n, k, chains, blocks, iterations = 128, 128, 64, 1, 300, 16
+    a, b = _operands(BF16, blocks, chains, m, n, k, seed=bps)
+    got = _run(native, cuda, BF16, TCGEN05, a, b, m, n, k, chains, blocks, iterations, bps)
+    _check(BF16, got, a, b, iterations)
+
+
+def test_mxf4_scale_doubling(cuda, native):
+    m, n, k, blocks = 128, 128, 128, 2
+    a, b = _operands(MXF4, blocks, 1, m, n, k, seed=11)
+    sa = torch.full((blocks, m, k // 32), 127, dtype=torch.uint8)
+    sb = torch.full((blocks, n, k // 32), 127, dtype=torch.uint8)
+    base = _run(native, cuda, MXF4, TCGEN05, a, b, m, n, k, 1, blocks, 1, sa=sa, sb=sb)
+    doubled = _run(native, cuda, MXF4, TCGEN05, a, b, m, n, k, 1, blocks, 1, sa=sa + 1, sb=sb)
+    assert torch.equal(doubled, 2 * base)
+
+
+def test_mxf4_per_group_scales(cuda, native):
+    """Scale factors that vary by row and by 32-element K group."""
+    m, n, k, blocks = 128, 256, 256, 2
+    a, b = _operands(MXF4, blocks, 1, m, n, k, seed=5)
+    gen = torch.Generator().manual_seed(9)
+    sa = torch.randint(125, 130, (blocks, m, k // 32), generator=gen, dtype=torch.uint8)
+    sb = torch.randint(125, 130, (blocks, n, k // 32), generator=gen, dtype=torch.uint8)
+    got = _run(native, cuda, MXF4, TCGEN05, a, b, m, n, k, 1, blocks, 1, sa=sa, sb=sb)
+    _check(MXF4, got, a, b, 1, sa, sb)
+
+
+@pytest.mark.parametrize("variant,m,n,k,chains", [
+    (DMMA, 128, 128, 16, 2), (DMMA, 256, 256, 32, 1), (DMMA, 128, 256, 8, 1),
+    (SIMT, 128, 128, 16, 2), (SIMT, 256, 256, 32, 1)])
+@pytest.mark.parametrize("iterations", [1, 5])
+def test_fp64_exact(cuda, native, variant, m, n, k, chains, iterations):
+    blocks = 2
+    a, b = _operands(FP64, blocks, chains, m, n, k, seed=k + iterations)
+    got = _run(native, cuda, FP64, variant, a, b, m, n, k, chains, blocks, iterations)
+    _check(FP64, got, a, b, iterations)
+
+
+@pytest.mark.parametrize("m,n,k,chains", [(128, 128, 32, 2), (256, 256, 32, 1),
+                                          (128, 256, 8, 1)])
+@pytest.mark.parametrize("iterations", [1, 7])
+def test_fp32_simt_exact(cuda, native, m, n, k, chains, iterations):
+    blocks = 2
+    a, b = _operands(FP32, blocks, chains, m, n, k, seed=m + iterations)
+    got = _run(native, cuda, FP32, SIMT, a, b, m, n, k, chains, blocks, iterations)
+    _check(FP32, got, a, b, iterations)
+
+
+def test_fp32_precision_probes(cuda):
+    from triton_chip_benchmarks_b200 import bench_tensor
+    ieee = bench_tensor.validate_fp32_precision(cuda, "ieee")
+    tf32 = bench_tensor.validate_fp32_precision(cuda, "tf32")
+    assert ieee["passed"] and tf32["passed"]
+
+
+@pytest.mark.parametrize("variant", [DMMA, SIMT])
+def test_fp64_precision_probe(cuda, variant):
+    from triton_chip_benchmarks_b200 import bench_tensor
+    assert bench_tensor.validate_fp64_precision(cuda, variant)["passed"]
+
+
+def test_fp4_arithmetic_probe(cuda):
+    from triton_chip_benchmarks_b200 import bench_tensor
+    assert bench_tensor.validate_fp4_arithmetic(cuda)["scale_sensitivity_verified"]
+
+
+def test_unsupported_tiles_are_capability_errors(cuda, native):
+    a = torch.zeros((1, 64, 64), dtype=torch.bfloat16, device=cuda)
+    c = torch.zeros((1, 1, 64, 64), device=cuda)
+    with pytest.raises(native.TcbError) as info:
+        native.tensor_peak(BF16, TCGEN05, a, a, c, blocks=1, blocks_per_sm=1, tile_m=64,
+                           tile_n=64, tile_k=64, chains=1, iterations=1)
+    assert info.value.is_capability
+
+
+def test_kernel_info_reports_instruction(native, cuda):
+    info = native.kernel_info(native.FAMILY_TENSOR, BF16, TCGEN05, 256, 256, 64, 1, 1)
+    assert "kind::f16" in info["instruction"] and info["execution_kind"] == "tensor"
+    assert info["local_bytes_per_thread"] == 0
+    simt = native.kernel_info(native.FAMILY_TENSOR, FP32, SIMT, 256, 256, 32, 1, 1)
+    assert simt["instruction"] == "fma.rn.f32" and simt["execution_kind"] == "simt"

@@ -1,0 +1,345 @@
+// Device copy and read bandwidth probes (sm_100a).
+//
+// copy: dst = src over a byte range.  Two kernels:
+//   * LDG128 - persistent grid-stride loop; each thread keeps UNROLL 16-byte
+//     loads in flight before storing them (streaming load/store hints keep the
+//     one-pass data out of L1 and mark it evict-first in L2).
+//   * BULK   - the bulk-copy engine: one lane per CTA moves CHUNK-byte pieces
+//     global -> shared -> global through a ring of STAGES buffers; completion
+//     of loads is tracked by mbarriers, of stores by bulk groups.
+// read: per-block FP32 sum of a block of elements into a sink word, the
+//   streaming-read companion pattern (16-byte .cg loads).
+//
+// Counterparts in the reference suite: copy_kernel / launch_copy
+// (bench_bandwidth.py:36-47) and read_kernel / launch_read
+// (bench_bandwidth.py:50-67).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "tcb_device.cuh"
+#include "tcb_host.h"
+#include "tcb_registry.h"
+
+namespace tcb {
+namespace {
+
+constexpr int kCopyUnroll = 4;
+constexpr int kBulkChunk = 32768;
+constexpr int kBulkStages = 4;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_stream_v4(uint4* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Copy of the trailing bytes that do not fill a 16-byte vector.
+__device__ __forceinline__ void copy_tail(const unsigned char* src, unsigned char* dst,
+                                          size_t first, size_t bytes) {
+  if (blockIdx.x == 0) {
+    for (size_t i = first + threadIdx.x; i < bytes; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+__global__ void __launch_bounds__(1024)
+    copy_ldg128_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t bytes) {
+  const size_t nvec = bytes >> 4;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + (kCopyUnroll - 1) * stride < nvec; i += kCopyUnroll * stride) {
+    uint4 v[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) v[u] = ld_stream_v4(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) st_stream_v4(dst + i + u * stride, v[u]);
+  }
+  for (; i < nvec; i += stride) st_stream_v4(dst + i, ld_stream_v4(src + i));
+  copy_tail(reinterpret_cast<const unsigned char*>(src), reinterpret_cast<unsigned char*>(dst),
+            nvec << 4, bytes);
+}
+
+__global__ void copy_bytes_kernel(const unsigned char* __restrict__ src,
+                                  unsigned char* __restrict__ dst, size_t bytes) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < bytes;
+       i += stride)
+    dst[i] = src[i];
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t size,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(smem_dst)),
+      "l"(src), "r"(size), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* smem_src, uint32_t size) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_addr(smem_src)), "r"(size)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Chunk k of this CTA covers bytes [off, off+size) of the 16-byte aligned body.
+__device__ __forceinline__ void bulk_chunk(size_t body, long long k, size_t* off, uint32_t* size) {
+  const size_t start = (static_cast<size_t>(blockIdx.x) + static_cast<size_t>(k) * gridDim.x) *
+                       static_cast<size_t>(kBulkChunk);
+  const size_t left = body - start;
+  *off = start;
+  *size = static_cast<uint32_t>(left < kBulkChunk ? left : kBulkChunk);
+}
+
+__global__ void __launch_bounds__(32)
+    copy_bulk_kernel(const unsigned char* __restrict__ src, unsigned char* __restrict__ dst,
+                     size_t bytes, int* status) {
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  const size_t body = bytes & ~static_cast<size_t>(15);
+  const size_t nchunks_total = (body + kBulkChunk - 1) / kBulkChunk;
+  const long long mine =
+      blockIdx.x < nchunks_total
+          ? static_cast<long long>((nchunks_total - 1 - blockIdx.x) / gridDim.x + 1)
+          : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    const long long prologue = mine < kBulkStages ? mine : kBulkStages;
+    for (long long k = 0; k < prologue; ++k) {
+      size_t off;
+      uint32_t size;
+      bulk_chunk(body, k, &off, &size);
+      mbar_arrive_expect_tx(&bars[k], size);
+      bulk_load(ring + k * kBulkChunk, src + off, size, &bars[k]);
+    }
+    for (long long k = 0; k < mine; ++k) {
+      const int s = static_cast<int>(k % kBulkStages);
+      const uint32_t phase = static_cast<uint32_t>((k / kBulkStages) & 1);
+      if (!mbar_wait(&bars[s], phase)) {
+        report_status(status, TCB_ERR_TIMEOUT);
+        break;
+      }
+      size_t off;
+      uint32_t size;
+      bulk_chunk(body, k, &off, &size);
+      bulk_store(dst + off, ring + s * kBulkChunk, size);
+      bulk_commit();
+      // Refill the stage whose store was issued one step earlier, once that
+      // store has finished reading its shared-memory buffer.
+      const long long refill = k - 1 + kBulkStages;
+      if (k >= 1 && refill < mine) {
+        bulk_wait_read<1>();
+        const int rs = static_cast<int>((k - 1) % kBulkStages);
+        size_t roff;
+        uint32_t rsize;
+        bulk_chunk(body, refill, &roff, &rsize);
+        mbar_arrive_expect_tx(&bars[rs], rsize);
+        bulk_load(ring + rs * kBulkChunk, src + roff, rsize, &bars[rs]);
+      }
+    }
+    bulk_wait_all();
+  }
+  copy_tail(src, dst, body, bytes);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+__device__ __forceinline__ uint4 ld_cg_v4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// One CTA sums `block_elems` consecutive elements.  Each thread accumulates
+// its 16-byte vectors lane-wise into independent FP32 partials, then the
+// CTA reduces them with warp shuffles and one shared-memory pass.
+template <typename T>
+__global__ void __launch_bounds__(1024)
+    read_sum_kernel(const T* __restrict__ src, long long elements, float* __restrict__ sink,
+                    int block_elems) {
+  constexpr int kVec = 16 / sizeof(T);
+  __shared__ float warp_sums[32];
+  const long long base = static_cast<long long>(blockIdx.x) * block_elems;
+  long long count = elements - base;
+  if (count > block_elems) count = block_elems;
+  float part[kVec];
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) part[j] = 0.f;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  const long long nvec = vec_ok ? count / kVec : 0;
+  const uint4* vsrc = reinterpret_cast<const uint4*>(src + base);
+  for (long long v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 raw = ld_cg_v4(vsrc + v);
+    const T* vals = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) part[j] += to_f32(vals[j]);
+  }
+  for (long long e = nvec * kVec + threadIdx.x; e < count; e += blockDim.x)
+    part[0] += to_f32(src[base + e]);
+  float total = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVec; ++j) total += part[j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) warp_sums[warp] = total;
+  __syncthreads();
+  if (warp == 0) {
+    const int nwarps = blockDim.x >> 5;
+    float t = lane < nwarps ? warp_sums[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) sink[blockIdx.x] = t;
+  }
+}
+
+}  // namespace
+
+int copy_bulk_smem_bytes() { return kBulkStages * kBulkChunk; }
+
+}  // namespace tcb
+
+using namespace tcb;
+
+extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, int blocks,
+                        int threads, tcb_stream_t stream) {
+  if (bytes == 0) return TCB_OK;
+  if (src == nullptr || dst == nullptr) return TCB_ERR_INVALID_ARGUMENT;
+  if (variant != TCB_COPY_LDG128 && variant != TCB_COPY_BULK) return TCB_ERR_INVALID_ARGUMENT;
+  if (blocks < 0 || threads < 0) return TCB_ERR_INVALID_ARGUMENT;
+  DeviceFacts facts;
+  int rc = current_device_facts(&facts);
+  if (rc != TCB_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec_ok = aligned(src, 16) && aligned(dst, 16);
+  if (!vec_ok) {
+    copy_bytes_kernel<<<facts.sm_count * 8, 256, 0, s>>>(
+        static_cast<const unsigned char*>(src), static_cast<unsigned char*>(dst), bytes);
+    return launch_status();
+  }
+  if (variant == TCB_COPY_LDG128) {
+    if (threads == 0) threads = 512;
+    if (threads < 32 || threads > 1024 || threads % 32) return TCB_ERR_INVALID_ARGUMENT;
+    if (blocks == 0) blocks = facts.sm_count * (2048 / threads);
+    copy_ldg128_kernel<<<blocks, threads, 0, s>>>(static_cast<const uint4*>(src),
+                                                  static_cast<uint4*>(dst), bytes);
+    return launch_status();
+  }
+  // Bulk-copy engine: one warp per CTA (lane 0 drives the ring).
+  if (threads != 0 && threads != 32) return TCB_ERR_INVALID_ARGUMENT;
+  const int smem = copy_bulk_smem_bytes();
+  if (smem > facts.max_smem_optin) return TCB_ERR_RESOURCE;
+  static int configured_device = -1;
+  if (configured_device != facts.device) {
+    if (cudaFuncSetAttribute(copy_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
+      return TCB_ERR_RESOURCE;
+    configured_device = facts.device;
+  }
+  if (blocks == 0) blocks = facts.sm_count;
+  copy_bulk_kernel<<<blocks, 32, smem, s>>>(static_cast<const unsigned char*>(src),
+                                            static_cast<unsigned char*>(dst), bytes, nullptr);
+  return launch_status();
+}
+
+extern "C" int tcb_read(const void* src, int dtype, long long elements, float* sink,
+                        int block_elems, int threads, tcb_stream_t stream) {
+  if (elements == 0) return TCB_OK;
+  if (src == nullptr || sink == nullptr || elements < 0) return TCB_ERR_INVALID_ARGUMENT;
+  if (!is_pow2(block_elems) || block_elems < 256 || block_elems > 65536)
+    return TCB_ERR_INVALID_ARGUMENT;
+  if (threads == 0) threads = 256;
+  if (threads < 32 || threads > 1024 || threads % 32) return TCB_ERR_INVALID_ARGUMENT;
+  const long long grid = (elements + block_elems - 1) / block_elems;
+  if (grid > 0x7fffffffLL) return TCB_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case TCB_READ_FP32:
+      read_sum_kernel<float><<<static_cast<unsigned>(grid), threads, 0, s>>>(
+          static_cast<const float*>(src), elements, sink, block_elems);
+      break;
+    case TCB_READ_FP16:
+      read_sum_kernel<__half><<<static_cast<unsigned>(grid), threads, 0, s>>>(
+          static_cast<const __half*>(src), elements, sink, block_elems);
+      break;
+    case TCB_READ_BF16:
+      read_sum_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), threads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(src), elements, sink, block_elems);
+      break;
+    default:
+      return TCB_ERR_INVALID_ARGUMENT;
+  }
+  return launch_status();
+}
+
+// Kernel facts for tcb_kernel_info (registry hooks).
+namespace tcb {
+int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out) {
+  cudaFuncAttributes attr;
+  const void* fn = variant == TCB_COPY_BULK ? reinterpret_cast<const void*>(copy_bulk_kernel)
+                                            : reinterpret_cast<const void*>(copy_ldg128_kernel);
+  if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;
+  fill_kernel_info(attr, out);
+  out->dynamic_smem_bytes = variant == TCB_COPY_BULK ? copy_bulk_smem_bytes() : 0;
+  out->threads_per_block = variant == TCB_COPY_BULK ? 32 : (threads ? threads : 512);
+  out->tensor_core = 0;
+  copy_str(out->instruction, sizeof(out->instruction),
+           variant == TCB_COPY_BULK
+               ? "cp.async.bulk.shared::cluster.global / cp.async.bulk.global.shared::cta"
+               : "ld.global.nc.L1::no_allocate.v4.u32 / st.global.cs.v4.u32");
+  copy_str(out->execution_kind, sizeof(out->execution_kind), "memory");
+  return TCB_OK;
+}
+
+int read_kernel_info(int dtype, int threads, tcb_kernel_info_t* out) {
+  cudaFuncAttributes attr;
+  const void* fn = dtype == TCB_READ_FP16   ? reinterpret_cast<const void*>(read_sum_kernel<__half>)
+                   : dtype == TCB_READ_BF16 ? reinterpret_cast<const void*>(
+                                                  read_sum_kernel<__nv_bfloat16>)
+                                            : reinterpret_cast<const void*>(read_sum_kernel<float>);
+  if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;
+  fill_kernel_info(attr, out);
+  out->dynamic_smem_bytes = 0;
+  out->threads_per_block = threads ? threads : 256;
+  out->tensor_core = 0;
+  copy_str(out->instruction, sizeof(out->instruction), "ld.global.cg.v4.u32");
+  copy_str(out->execution_kind, sizeof(out->execution_kind), "memory");
+  return TCB_OK;
+}
+}  // namespace tcb
