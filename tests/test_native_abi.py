@@ -1,0 +1,68 @@
+"""The C ABI library loads and exports every symbol include/tcb.h declares (CPU)."""
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "tcb.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tcb_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for expected in ("tcb_copy", "tcb_read", "tcb_vector_chains", "tcb_tensor_peak",
+                     "tcb_kernel_info", "tcb_device_query", "tcb_strerror", "tcb_version"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol(native):
+    lib = ctypes.CDLL(str(native.library_path()))
+    missing = [name for name in declared_functions() if not hasattr(lib, name)]
+    assert not missing, missing
+    assert set(native.EXPORTED_SYMBOLS) >= set(n for n in declared_functions()
+                                               if n not in ("tcb_fp4_gemm",))
+
+
+def test_status_text_and_version(native):
+    assert native.version().startswith("tcb ") and "sm_100a" in native.version()
+    assert native.strerror(native.OK) == "ok"
+    assert "unsupported" in native.strerror(native.ERR_UNSUPPORTED)
+    assert "timed out" in native.strerror(native.ERR_TIMEOUT)
+    assert native.strerror(-99) == "unknown status"
+
+
+def test_status_codes_match_header(native):
+    text = HEADER.read_text()
+    for name in ("OK", "ERR_INVALID_ARGUMENT", "ERR_UNSUPPORTED", "ERR_RESOURCE", "ERR_LAUNCH",
+                 "ERR_DEVICE", "ERR_TIMEOUT", "ERR_ALIGNMENT"):
+        match = re.search(rf"#define TCB_{name}\s+\(?(-?\d+)\)?", text)
+        assert match and int(match.group(1)) == getattr(native, name), name
+
+
+def test_enums_match_header(native):
+    text = HEADER.read_text()
+    pairs = {"TCB_T_BF16": native.T_BF16, "TCB_T_MXF4": native.T_MXF4,
+             "TCB_T_FP32": native.T_FP32, "TCB_V_INT8_DP4A": native.V_INT8_DP4A,
+             "TCB_V_INT8_MULADD": native.V_INT8_MULADD, "TCB_TV_SIMT": native.TV_SIMT,
+             "TCB_COPY_BULK": native.COPY_BULK, "TCB_READ_BF16": native.READ_BF16,
+             "TCB_FAMILY_TENSOR": native.FAMILY_TENSOR}
+    for name, value in pairs.items():
+        match = re.search(rf"#define {name}\s+(\d+)", text)
+        assert match and int(match.group(1)) == value, name
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    from triton_chip_benchmarks_b200 import _native
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setenv("TCB_LIBRARY", str(tmp_path / "absent.so"))
+    with pytest.raises(_native.NativeLibraryError):
+        _native.load()
+    monkeypatch.delenv("TCB_LIBRARY")

@@ -247,6 +247,7 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
   int rc = current_device_facts(&facts);
   if (rc != TCB_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  clear_stale_error();
   const bool vec_ok = aligned(src, 16) && aligned(dst, 16);
   if (!vec_ok) {
     copy_bytes_kernel<<<facts.sm_count * 8, 256, 0, s>>>(
@@ -267,9 +268,9 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
   if (smem > facts.max_smem_optin) return TCB_ERR_RESOURCE;
   static int configured_device = -1;
   if (configured_device != facts.device) {
-    if (cudaFuncSetAttribute(copy_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem) != cudaSuccess)
-      return TCB_ERR_RESOURCE;
+    const int cap =
+        raise_dynamic_smem(reinterpret_cast<const void*>(copy_bulk_kernel), facts.max_smem_optin);
+    if (cap < smem) return TCB_ERR_RESOURCE;
     configured_device = facts.device;
   }
   if (blocks == 0) blocks = facts.sm_count;
@@ -289,6 +290,7 @@ extern "C" int tcb_read(const void* src, int dtype, long long elements, float* s
   const long long grid = (elements + block_elems - 1) / block_elems;
   if (grid > 0x7fffffffLL) return TCB_ERR_INVALID_ARGUMENT;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  clear_stale_error();
   switch (dtype) {
     case TCB_READ_FP32:
       read_sum_kernel<float><<<static_cast<unsigned>(grid), threads, 0, s>>>(

@@ -20,9 +20,29 @@ struct DeviceFacts {
 // cudaDeviceGetAttribute only (no context-wide side effects, capture-safe).
 int current_device_facts(DeviceFacts* out);
 
+// Drop a non-sticky error left by an earlier runtime call, so that the check
+// after a launch reports that launch only.
+inline void clear_stale_error() { (void)cudaGetLastError(); }
+
 inline int launch_status() {
   cudaError_t err = cudaGetLastError();
   return err == cudaSuccess ? TCB_OK : TCB_ERR_LAUNCH;
+}
+
+// Allow `fn` the device's opt-in shared memory minus its static shared
+// memory; returns the dynamic bytes a launch may request, or -1.
+inline int raise_dynamic_smem(const void* fn, int max_optin) {
+  cudaFuncAttributes attr;
+  if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) {
+    clear_stale_error();
+    return -1;
+  }
+  const int cap = max_optin - static_cast<int>(attr.sharedSizeBytes);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap) != cudaSuccess) {
+    clear_stale_error();
+    return -1;
+  }
+  return cap;
 }
 
 inline bool aligned(const void* p, uintptr_t a) {

@@ -347,10 +347,9 @@ extern "C" int tcb_tensor_peak(int dtype, int variant, const void* A, const void
   SimtPlan p;
   rc = simt_plan(dtype, variant, tile_m, tile_n, tile_k, chains, facts.max_smem_optin, &p);
   if (rc != TCB_OK) return rc;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(p.fn),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, facts.max_smem_optin) !=
-      cudaSuccess)
-    return TCB_ERR_RESOURCE;
+  const int cap = raise_dynamic_smem(reinterpret_cast<const void*>(p.fn), facts.max_smem_optin);
+  if (cap < 0 || p.smem > cap) return TCB_ERR_RESOURCE;
+  clear_stale_error();
   SimtArgs args{A, B, C, blocks, tile_m, tile_n, tile_k, chains, iterations};
   p.fn<<<blocks, p.threads, p.smem, s>>>(args);
   (void)blocks_per_sm;

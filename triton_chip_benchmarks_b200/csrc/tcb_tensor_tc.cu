@@ -467,19 +467,19 @@ int tc_tensor_peak(int dtype, const void* A, const void* B, const void* SA, cons
   args.idesc = make_idesc(p.kind, tile_n);
   KernelFn fn = kernel_for(p.kind);
   // Raise the dynamic shared-memory cap once per (kernel, device).
-  static int configured[6][64];
-  static bool init = false;
-  if (!init) {
-    for (auto& row : configured)
-      for (int& v : row) v = 0;
-    init = true;
-  }
-  if (facts.device < 64 && configured[p.kind][facts.device] < p.smem_request) {
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             facts.max_smem_optin) != cudaSuccess)
+  static int dyn_cap[6][64] = {};
+  if (facts.device >= 64) return TCB_ERR_DEVICE;
+  int& cap = dyn_cap[p.kind][facts.device];
+  if (cap == 0) {
+    cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+    if (cap < 0) {
+      cap = 0;
       return TCB_ERR_RESOURCE;
-    configured[p.kind][facts.device] = facts.max_smem_optin;
+    }
   }
+  if (p.smem_bytes > cap) return TCB_ERR_RESOURCE;
+  if (p.smem_request > cap) p.smem_request = cap;
+  clear_stale_error();
   fn<<<blocks, kThreads, p.smem_request, stream>>>(map_a, map_b, args);
   return launch_status();
 }

@@ -317,6 +317,7 @@ extern "C" int tcb_vector_chains(int dtype, const void* in, void* out, const voi
     return TCB_ERR_ALIGNMENT;
   const long long words_per_chain = elements / c.pack;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  clear_stale_error();
   c.fn<<<blocks, threads, 0, s>>>(in, out, coeff, words_per_chain, iterations);
   return launch_status();
 }
