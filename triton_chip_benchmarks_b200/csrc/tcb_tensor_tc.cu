@@ -77,15 +77,49 @@ __device__ __forceinline__ void mma_issue(uint32_t d, uint64_t adesc, uint64_t b
   }
 }
 
-// Byte offset of k-step s inside a K-major operand of `rows` rows stored as
-// consecutive panels of `panel` bytes per row.
-__device__ __forceinline__ uint32_t kstep_offset(int s, int rows, int panel) {
-  const int kb = s * kMmaKBytes;
-  const int p = kb / panel;
-  return static_cast<uint32_t>(p * rows * panel + (kb - p * panel));
+// Maximum (half, chain) accumulator groups resident at once: 2 halves x 2 chains.
+constexpr int kMaxGroups = 4;
+
+// Single-thread MMA issue over the resident tiles for one pass, specialised on
+// the K-steps per tile (KSTEPS) and the panel width (PANEL bytes) so that the
+// per-MMA work is an add on the descriptor's address field and the issue.
+// Operand j of group gi starts at a_lo[gi] (16-byte units); k-step s of a
+// K-major operand with `rows` rows sits at panel s*32/PANEL, column
+// (s*32) % PANEL.
+template <int KIND, int KSTEPS, int PANEL>
+__device__ __forceinline__ void issue_pass(const uint32_t (&d)[kMaxGroups],
+                                           const uint32_t (&a_lo)[kMaxGroups],
+                                           const uint32_t (&b_lo)[kMaxGroups],
+                                           const uint32_t (&sfa)[kMaxGroups], uint32_t sfb,
+                                           int groups, int rows_a, int rows_b, int iterations,
+                                           uint64_t desc_const, uint32_t idesc,
+                                           uint32_t sf_step_cols) {
+  uint32_t a_off[KSTEPS], b_off[KSTEPS];
+#pragma unroll
+  for (int s = 0; s < KSTEPS; ++s) {
+    constexpr int kStepsPerPanel = PANEL / kMmaKBytes;
+    const int p = s / kStepsPerPanel, w = (s % kStepsPerPanel) * kMmaKBytes;
+    a_off[s] = static_cast<uint32_t>(p * rows_a * PANEL + w) >> 4;
+    b_off[s] = static_cast<uint32_t>(p * rows_b * PANEL + w) >> 4;
+  }
+#pragma unroll 1
+  for (int it = 0; it < iterations; ++it) {
+#pragma unroll
+    for (int gi = 0; gi < kMaxGroups; ++gi) {
+      if (gi < groups) {
+#pragma unroll
+        for (int s = 0; s < KSTEPS; ++s) {
+          const uint64_t ad = desc_const | (a_lo[gi] + a_off[s]);
+          const uint64_t bd = desc_const | (b_lo[gi] + b_off[s]);
+          mma_issue<KIND>(d[gi], ad, bd, idesc, s != 0 || it != 0,
+                          sfa[gi] + s * sf_step_cols, sfb + s * sf_step_cols);
+        }
+      }
+    }
+  }
 }
 
-template <int KIND>
+template <int KIND, int KSTEPS, int PANEL>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_peak_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, const TcArgs args) {
@@ -99,8 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.x;
-  const int M = args.tile_m, N = args.tile_n, panel = args.panel;
-  const int panels = args.kbytes / panel;
+  const int M = args.tile_m, N = args.tile_n, panel = PANEL;
+  const int panels = args.kbytes / PANEL;
   uint8_t* sA = smem;
   uint8_t* sB = smem + M * args.kbytes;
 
@@ -167,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
 
   const uint32_t a0 = smem_addr(sA), b0 = smem_addr(sB);
-  const uint64_t desc_hi = smem_desc(0, 16, static_cast<uint32_t>(8 * panel), args.layout);
+  const uint64_t desc_const = smem_desc(0, 16, static_cast<uint32_t>(8 * PANEL), args.layout);
   const int passes = (args.groups + args.groups_per_pass - 1) / args.groups_per_pass;
   for (int pass = 0; ok && pass < passes; ++pass) {
     const int g0 = pass * args.groups_per_pass;
@@ -176,21 +210,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
       if (lane == 0) {
         tc_fence_after();
-        for (int it = 0; it < args.iterations; ++it) {
-          for (int g = g0; g < g1; ++g) {
-            const int c = g / args.halves, h = g - c * args.halves;
-            const uint32_t d = tbase + static_cast<uint32_t>((g - g0) * N);
-            const uint32_t a_half = a0 + static_cast<uint32_t>(h * 128 * panel);
-            const uint32_t b_chain = b0 + static_cast<uint32_t>(c * panels * N * panel);
-            for (int s = 0; s < args.ksteps; ++s) {
-              const uint64_t ad = desc_hi | (((a_half + kstep_offset(s, M, panel)) >> 4) & 0x3FFFu);
-              const uint64_t bd = desc_hi | (((b_chain + kstep_offset(s, N, panel)) >> 4) & 0x3FFFu);
-              const uint32_t sfc = tbase + static_cast<uint32_t>(sf_base + s * sf_step_cols);
-              mma_issue<KIND>(d, ad, bd, args.idesc, (it | s) != 0, sfc + 4 * h,
-                              sfc + 4 * args.halves);
-            }
-          }
+        uint32_t d[kMaxGroups], a_lo[kMaxGroups], b_lo[kMaxGroups], sfa[kMaxGroups];
+#pragma unroll
+        for (int gi = 0; gi < kMaxGroups; ++gi) {
+          const int g = min(g0 + gi, args.groups - 1);
+          const int c = g / args.halves, h = g - c * args.halves;
+          d[gi] = tbase + static_cast<uint32_t>(gi * N);
+          a_lo[gi] = (a0 + static_cast<uint32_t>(h * 128 * PANEL)) >> 4;
+          b_lo[gi] = (b0 + static_cast<uint32_t>(c * panels * N * PANEL)) >> 4;
+          sfa[gi] = tbase + static_cast<uint32_t>(sf_base + 4 * h);
         }
+        const uint32_t sfb = tbase + static_cast<uint32_t>(sf_base + 4 * args.halves);
+        issue_pass<KIND, KSTEPS, PANEL>(d, a_lo, b_lo, sfa, sfb, g1 - g0, M, N, args.iterations,
+                                        desc_const, args.idesc,
+                                        static_cast<uint32_t>(sf_step_cols));
         tc_commit(&bar_mma);
       }
       __syncwarp();
@@ -237,22 +270,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- host side
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
 
-KernelFn kernel_for(int kind) {
-  switch (kind) {
-    case kF16:
-      return tc_peak_kernel<kF16>;
-    case kBF16:
-      return tc_peak_kernel<kBF16>;
-    case kTF32:
-      return tc_peak_kernel<kTF32>;
-    case kI8:
-      return tc_peak_kernel<kI8>;
-    case kE4M3:
-      return tc_peak_kernel<kE4M3>;
-    case kMXF4:
-      return tc_peak_kernel<kMXF4>;
+// (KSTEPS, PANEL) pairs: K bytes per row of 32, 64, 128, 256, 512 and 1024.
+template <int KIND>
+KernelFn kernel_for_steps(int ksteps) {
+  switch (ksteps) {
+    case 1: return tc_peak_kernel<KIND, 1, 32>;
+    case 2: return tc_peak_kernel<KIND, 2, 64>;
+    case 4: return tc_peak_kernel<KIND, 4, 128>;
+    case 8: return tc_peak_kernel<KIND, 8, 128>;
+    case 16: return tc_peak_kernel<KIND, 16, 128>;
+    case 32: return tc_peak_kernel<KIND, 32, 128>;
   }
   return nullptr;
+}
+
+KernelFn kernel_for(int kind, int ksteps) {
+  switch (kind) {
+    case kF16: return kernel_for_steps<kF16>(ksteps);
+    case kBF16: return kernel_for_steps<kBF16>(ksteps);
+    case kTF32: return kernel_for_steps<kTF32>(ksteps);
+    case kI8: return kernel_for_steps<kI8>(ksteps);
+    case kE4M3: return kernel_for_steps<kE4M3>(ksteps);
+    case kMXF4: return kernel_for_steps<kMXF4>(ksteps);
+  }
+  return nullptr;
+}
+
+int steps_index(int ksteps) {
+  switch (ksteps) {
+    case 1: return 0;
+    case 2: return 1;
+    case 4: return 2;
+    case 8: return 3;
+    case 16: return 4;
+    case 32: return 5;
+  }
+  return -1;
 }
 
 const char* instruction_for(int kind) {
@@ -385,6 +438,7 @@ int make_plan(int dtype, int tile_m, int tile_n, int tile_k, int chains, int bps
   if (acc_cols < tile_n) return TCB_ERR_RESOURCE;
   p.groups_per_pass = acc_cols / tile_n;
   if (p.groups_per_pass > p.groups) p.groups_per_pass = p.groups;
+  if (p.groups_per_pass > kMaxGroups) p.groups_per_pass = kMaxGroups;
   p.smem_bytes = (tile_m + chains * tile_n) * p.kbytes + 1024;
   const int floor_bytes = kSmemPerSM / (bps + 1) + 1;
   p.smem_request = p.smem_bytes > floor_bytes ? p.smem_bytes : floor_bytes;
@@ -465,11 +519,12 @@ int tc_tensor_peak(int dtype, const void* A, const void* B, const void* SA, cons
   args.sf_groups = p.ksteps * 2;
   args.layout = p.layout;
   args.idesc = make_idesc(p.kind, tile_n);
-  KernelFn fn = kernel_for(p.kind);
+  KernelFn fn = kernel_for(p.kind, p.ksteps);
+  if (fn == nullptr) return TCB_ERR_UNSUPPORTED;
   // Raise the dynamic shared-memory cap once per (kernel, device).
-  static int dyn_cap[6][64] = {};
+  static int dyn_cap[6][6][64] = {};
   if (facts.device >= 64) return TCB_ERR_DEVICE;
-  int& cap = dyn_cap[p.kind][facts.device];
+  int& cap = dyn_cap[p.kind][steps_index(p.ksteps)][facts.device];
   if (cap == 0) {
     cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
     if (cap < 0) {
@@ -493,8 +548,9 @@ int tc_kernel_info(int dtype, int tile_m, int tile_n, int tile_k, int chains, in
   rc = make_plan(dtype, tile_m, tile_n, tile_k, chains, bps, facts.max_smem_optin, &p);
   if (rc != TCB_OK) return rc;
   cudaFuncAttributes attr;
-  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(kernel_for(p.kind))) !=
-      cudaSuccess)
+  KernelFn fn = kernel_for(p.kind, p.ksteps);
+  if (fn == nullptr) return TCB_ERR_UNSUPPORTED;
+  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(fn)) != cudaSuccess)
     return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
   out->dynamic_smem_bytes = p.smem_request;
