@@ -21,9 +21,7 @@ import argparse
 import json
 import os
 from pathlib import Path
-import statistics
 import sys
-import threading
 import time
 
 REPO = Path(__file__).resolve().parent
@@ -41,7 +39,9 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="ldg128")
+    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
+    parser.add_argument("--buffer-mib", type=int, default=BUFFER_BYTES >> 20,
+                        help="buffer size (default: the 4 GiB workload; smaller only for profiling)")
     parser.add_argument("--threads", type=int, default=512)
     parser.add_argument("--blocks", type=int, default=0, help="CTAs (0: library default)")
     parser.add_argument("--e2e-steps", type=int, default=3,
@@ -93,64 +93,6 @@ def all_sum(dist, value: float) -> float:
     return float(t.item())
 
 
-# ------------------------------------------------------------------ clocks
-class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML (read-only)."""
-
-    REASONS = {
-        0x0000000000000004: "sw_power_cap", 0x0000000000000008: "hw_slowdown",
-        0x0000000000000020: "sw_thermal_slowdown", 0x0000000000000040: "hw_thermal_slowdown",
-        0x0000000000000080: "hw_power_brake_slowdown", 0x0000000000000002: "applications_clocks_setting",
-        0x0000000000000100: "display_clock_setting",
-    }
-
-    def __init__(self, device_index: int, period_s: float = 0.002):
-        self.samples, self.reasons = [], set()
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        self.period = period_s
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-            index = int(visible.split(",")[device_index]) if visible else device_index
-            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
-        except Exception as exc:  # noqa: BLE001 - clocks are reported as unavailable
-            self._nvml = None
-            self.error = str(exc)
-
-    def _run(self):
-        nv = self._nvml
-        while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
-                for bit, name in self.REASONS.items():
-                    if mask & bit:
-                        self.reasons.add(name)
-            except Exception:  # noqa: BLE001
-                pass
-            time.sleep(self.period)
-
-    def start(self):
-        if self._nvml is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
-
-    def stop(self) -> dict:
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join()
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                    "samples": 0, "source": "nvml"}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
-
-
 # --------------------------------------------------------------- baselines
 def measured_peaks() -> dict:
     path = REPO / "MEASURED_PEAKS.json"
@@ -200,6 +142,7 @@ def run_ours(args):
     import torch
 
     from triton_chip_benchmarks_b200 import _native
+    from triton_chip_benchmarks_b200.clocks import ClockSampler
 
     world, rank, local = dist_env()
     dist = init_group(world)
@@ -208,13 +151,14 @@ def run_ours(args):
     variant = {"ldg128": _native.COPY_LDG128, "bulk": _native.COPY_BULK}[args.variant]
     threads = args.threads if args.variant == "ldg128" else 32
 
+    nbytes = args.buffer_mib << 20
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
-    src = torch.randint(0, 256, (BUFFER_BYTES,), dtype=torch.uint8, device=device, generator=gen)
+    src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=device, generator=gen)
     dst = torch.zeros_like(src)
     stream = torch.cuda.current_stream()
 
     def step():
-        _native.copy(src, dst, BUFFER_BYTES, variant, args.blocks, threads, stream)
+        _native.copy(src, dst, nbytes, variant, args.blocks, threads, stream)
 
     step()
     torch.cuda.synchronize()
@@ -227,22 +171,21 @@ def run_ours(args):
     if not torch.equal(src, dst):
         raise AssertionError("copy validation failed after warmup")
 
-    sampler = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(dist)
     torch.cuda.synchronize()
-    sampler.start()
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    end.record(stream)
-    torch.cuda.synchronize()
-    clocks = sampler.stop()
+    with ClockSampler(local) as sampler:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    clocks = sampler.summary()
     barrier(dist)
     local_ms = start.elapsed_time(end)
     ms = all_max(dist, local_ms)
     ms_per_step = ms / args.steps
-    traffic = 2 * BUFFER_BYTES
+    traffic = 2 * nbytes
     value = world * traffic * args.steps / (ms / 1e3) / 1e9
 
     # End to end through the C ABI with host buffers: H2D of the step's input
@@ -261,9 +204,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(dist)
     e2e_ms = all_max(dist, e2e_start.elapsed_time(e2e_end))
-    if not torch.equal(host_src[: 1 << 24], host_dst[: 1 << 24]):
+    if args.e2e_steps and not torch.equal(host_src[: 1 << 24], host_dst[: 1 << 24]):
         raise AssertionError("end-to-end copy mismatch")
-    e2e_value = world * traffic * args.e2e_steps / (e2e_ms / 1e3) / 1e9
+    e2e_value = world * traffic * args.e2e_steps / (e2e_ms / 1e3) / 1e9 if args.e2e_steps else None
     del host_src, host_dst
 
     if rank != 0:
@@ -289,14 +232,16 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded random bytes)",
-        "config": {"workload": WORKLOAD, "buffer_bytes": BUFFER_BYTES,
+        "config": {"workload": WORKLOAD if nbytes == BUFFER_BYTES else
+                   f"profiling case: {args.buffer_mib} MiB copy (not the headline workload)",
+                   "buffer_bytes": nbytes,
                    "bytes_per_step": traffic, "kernel": kernel_name,
                    "threads_per_cta": threads, "ctas": args.blocks or "library default",
                    "l2": "no flush: inputs (4 GiB) larger than the 126 MB L2",
                    "parallelism": f"replicas x{world} (no collective)"},
         "roofline": roofline, "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": BUFFER_BYTES,
-                "d2h_bytes_per_step": BUFFER_BYTES, "steps": args.e2e_steps,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nbytes,
+                "d2h_bytes_per_step": nbytes, "steps": args.e2e_steps,
                 "path": "pinned host -> device, tcb_copy, device -> pinned host"},
         "gpu_launches": args.steps, "clocks": clocks,
     }
@@ -332,7 +277,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded random bytes)",
-        "config": {"workload": WORKLOAD, "buffer_bytes": BUFFER_BYTES, "bytes_per_step": traffic,
+        "config": {"workload": WORKLOAD if nbytes == BUFFER_BYTES else
+                   f"profiling case: {args.buffer_mib} MiB copy (not the headline workload)",
+                   "buffer_bytes": nbytes, "bytes_per_step": traffic,
                    "parallelism": "host threads on rank 0"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": "port",
                          "sample": f"full 4 GiB buffer per step, {used} host threads "

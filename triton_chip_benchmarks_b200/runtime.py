@@ -293,8 +293,22 @@ def _batch_samples(fn, args, api, use_graph):
 
 
 def measure(fn, args, api=None) -> dict:
-    """Device-event timing of ``fn`` (never a host wall clock)."""
-    api = api or _default_api()
+    """Device-event timing of ``fn`` (never a host wall clock).
+
+    With the default CUDA device API the SM clock and throttle reasons are
+    sampled during the timed batches and returned under ``clocks``.
+    """
+    if api is None:
+        from .clocks import ClockSampler
+        import torch
+        with ClockSampler(torch.cuda.current_device()) as sampler:
+            result = _measure(fn, args, _default_api())
+        result["clocks"] = sampler.summary()
+        return result
+    return _measure(fn, args, api)
+
+
+def _measure(fn, args, api) -> dict:
     if not all(callable(getattr(api, name, None)) for name in ("Event", "synchronize")):
         raise RuntimeError("The device API does not expose timed events")
     fn()  # first launch outside any capture and any sample
