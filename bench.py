@@ -42,7 +42,9 @@ def parse_args():
     parser.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
     parser.add_argument("--buffer-mib", type=int, default=BUFFER_BYTES >> 20,
                         help="buffer size (default: the 4 GiB workload; smaller only for profiling)")
-    parser.add_argument("--threads", type=int, default=512)
+    parser.add_argument("--threads", type=int, default=512, help="CTA size of the ldg128 kernel")
+    parser.add_argument("--stages", type=int, default=0,
+                        help="bulk kernel ring depth in 32 KiB chunks (0: library default)")
     parser.add_argument("--blocks", type=int, default=0, help="CTAs (0: library default)")
     parser.add_argument("--e2e-steps", type=int, default=3,
                         help="steps of the host-buffer end-to-end leg")
@@ -149,7 +151,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     variant = {"ldg128": _native.COPY_LDG128, "bulk": _native.COPY_BULK}[args.variant]
-    threads = args.threads if args.variant == "ldg128" else 32
+    threads = args.threads if args.variant == "ldg128" else args.stages
 
     nbytes = args.buffer_mib << 20
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
@@ -236,7 +238,9 @@ def run_ours(args):
                    f"profiling case: {args.buffer_mib} MiB copy (not the headline workload)",
                    "buffer_bytes": nbytes,
                    "bytes_per_step": traffic, "kernel": kernel_name,
-                   "threads_per_cta": threads, "ctas": args.blocks or "library default",
+                   "threads_per_cta": threads if args.variant == "ldg128" else 32,
+                   "bulk_ring_stages": threads if args.variant == "bulk" else None,
+                   "ctas": args.blocks or "library default",
                    "l2": "no flush: inputs (4 GiB) larger than the 126 MB L2",
                    "parallelism": f"replicas x{world} (no collective)"},
         "roofline": roofline, "cpu_baseline": cpu,

@@ -72,9 +72,12 @@ int tcb_device_query(int device, tcb_device_props *out);
 #define TCB_COPY_LDG128 0 /* persistent grid-stride 128-bit loads/stores */
 #define TCB_COPY_BULK 1   /* bulk-copy engine: global -> shared -> global, one lane per CTA */
 
-/* dst[0:bytes) = src[0:bytes).  blocks = 0 selects 4 x SM count; threads = 0
- * selects 512.  Any byte count and alignment is accepted; the vector path
- * needs 16-byte aligned pointers and falls back to a byte loop otherwise.
+/* dst[0:bytes) = src[0:bytes).  Any byte count and alignment is accepted;
+ * both kernels need 16-byte aligned pointers and otherwise fall back to a byte
+ * loop.  blocks = 0 selects the tuned grid for the variant.  For LDG128,
+ * `threads` is the CTA size (0: 512).  For BULK the CTA is one warp and
+ * `threads` is the depth of the shared-memory ring in 32 KiB chunks (2..8,
+ * 0: 4). src and dst must not overlap.
  * Replaces launch_copy (bench_bandwidth.py:43-47) and copy_kernel
  * (bench_bandwidth.py:36-40). */
 int tcb_copy(const void *src, void *dst, size_t bytes, int variant, int blocks, int threads,

@@ -48,12 +48,17 @@ def parse_args(argv=None):
                         help="Threads per CTA of the 128-bit copy kernel")
     parser.add_argument("--copy-variants", choices=list(COPY_VARIANTS), nargs="+",
                         default=list(COPY_VARIANTS), help="Copy kernels to measure")
+    parser.add_argument("--bulk-stages", type=positive_int, nargs="+", default=[2, 4],
+                        help="Shared-memory ring depths (32 KiB chunks) of the bulk-copy kernel")
+    parser.add_argument("--copy-blocks-per-sm", type=positive_int, nargs="+", default=[4],
+                        help="CTAs per SM of the copy kernels (grid = value x SMs)")
     parser.add_argument("--quick", action="store_true",
                         help="Smoke check: 8 MiB, one configuration per mode; not an HBM result")
     args = parser.parse_args(argv)
     if args.quick:
         args.sizes_mib, args.block_sizes, args.num_warps = [8], [1024], None
         args.copy_threads, args.copy_variants = [512], ["ldg128"]
+        args.bulk_stages, args.copy_blocks_per_sm = [4], [4]
     if any(b & (b - 1) or b > 65536 or b < 256 for b in args.block_sizes):
         parser.error("--block-sizes must be powers of two in [256, 65536]")
     if args.num_warps is None:
@@ -65,19 +70,23 @@ def parse_args(argv=None):
     return args
 
 
-def copy_configs(args):
+def copy_configs(args, sms: int):
     configs = []
-    for variant in args.copy_variants:
-        if variant == "ldg128":
-            configs += [{"variant": variant, "threads": t} for t in args.copy_threads]
-        else:
-            configs.append({"variant": variant, "threads": 32})
+    for per_sm in args.copy_blocks_per_sm:
+        for variant in args.copy_variants:
+            if variant == "ldg128":
+                configs += [{"variant": variant, "threads": t, "blocks": per_sm * sms}
+                            for t in args.copy_threads]
+            else:
+                configs += [{"variant": variant, "stages": st, "threads": 32,
+                             "blocks": per_sm * sms} for st in args.bulk_stages]
     return configs
 
 
 def launch_copy(src, dst, config):
+    knob = config["stages"] if config["variant"] == "bulk" else config["threads"]
     _native.copy(src, dst, src.numel() * src.element_size(), COPY_VARIANTS[config["variant"]],
-                 0, config["threads"])
+                 config.get("blocks", 0), knob)
 
 
 def launch_read(src, sink, block, warps, dtype_name):
@@ -98,7 +107,7 @@ def main(argv=None):
         modes = ["copy"]
     element_size = torch.empty((), dtype=dtype).element_size()
     l2_bytes = metadata["l2_cache_bytes"]
-    copies = copy_configs(args)
+    copies = copy_configs(args, metadata["sm_count"])
     reads = [(block, warps) for block in args.block_sizes for warps in args.num_warps]
 
     # Masked tails: sizes that do not fill a 16-byte vector or a block.
@@ -157,9 +166,12 @@ def main(argv=None):
                 correctness = {"correctness": "passed (full output and masked tail)"}
                 write_bytes = buffer_bytes
                 block, warps = config["threads"], config["threads"] // 32
-                label = f"{config['variant']}/{config['threads']}t"
+                knob = config["stages"] if config["variant"] == "bulk" else config["threads"]
+                label = (f"bulk/{config['stages']}st/{config['blocks']}b"
+                         if config["variant"] == "bulk"
+                         else f"ldg128/{config['threads']}t/{config['blocks']}b")
                 info = _native.kernel_info(_native.FAMILY_COPY, COPY_VARIANTS[config["variant"]],
-                                           config["threads"])
+                                           knob)
             else:
                 block, warps = config
                 sink = torch.full((-(-n // block),), float("nan"), device=device)
@@ -186,6 +198,9 @@ def main(argv=None):
             }
             if mode == "copy":
                 row["copy_variant"] = config["variant"]
+                row["blocks"] = config["blocks"]
+                if config["variant"] == "bulk":
+                    row["bulk_ring_stages"] = config["stages"]
             rows.append(row)
             print(f"{mode:4s} {size_mib:11d}   {label:16s} {timings['min_ms']:9.4f} "
                   f"{timings['median_ms']:11.4f} {peak_gbps:11.2f} {gbps:12.2f}", flush=True)

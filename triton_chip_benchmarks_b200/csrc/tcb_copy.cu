@@ -25,7 +25,8 @@ namespace {
 
 constexpr int kCopyUnroll = 4;
 constexpr int kBulkChunk = 32768;
-constexpr int kBulkStages = 4;
+constexpr int kBulkMaxStages = 8;
+constexpr int kBulkDefaultStages = 4;
 
 __device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
   uint4 v;
@@ -113,9 +114,9 @@ __device__ __forceinline__ void bulk_chunk(size_t body, long long k, size_t* off
 
 __global__ void __launch_bounds__(32)
     copy_bulk_kernel(const unsigned char* __restrict__ src, unsigned char* __restrict__ dst,
-                     size_t bytes, int* status) {
+                     size_t bytes, int stages, int* status) {
   extern __shared__ __align__(128) unsigned char ring[];
-  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  __shared__ __align__(8) uint64_t bars[kBulkMaxStages];
   const size_t body = bytes & ~static_cast<size_t>(15);
   const size_t nchunks_total = (body + kBulkChunk - 1) / kBulkChunk;
   const long long mine =
@@ -123,9 +124,9 @@ __global__ void __launch_bounds__(32)
           ? static_cast<long long>((nchunks_total - 1 - blockIdx.x) / gridDim.x + 1)
           : 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kBulkStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
-    const long long prologue = mine < kBulkStages ? mine : kBulkStages;
+    const long long prologue = mine < stages ? mine : stages;
     for (long long k = 0; k < prologue; ++k) {
       size_t off;
       uint32_t size;
@@ -134,8 +135,8 @@ __global__ void __launch_bounds__(32)
       bulk_load(ring + k * kBulkChunk, src + off, size, &bars[k]);
     }
     for (long long k = 0; k < mine; ++k) {
-      const int s = static_cast<int>(k % kBulkStages);
-      const uint32_t phase = static_cast<uint32_t>((k / kBulkStages) & 1);
+      const int s = static_cast<int>(k % stages);
+      const uint32_t phase = static_cast<uint32_t>((k / stages) & 1);
       if (!mbar_wait(&bars[s], phase)) {
         report_status(status, TCB_ERR_TIMEOUT);
         break;
@@ -147,10 +148,10 @@ __global__ void __launch_bounds__(32)
       bulk_commit();
       // Refill the stage whose store was issued one step earlier, once that
       // store has finished reading its shared-memory buffer.
-      const long long refill = k - 1 + kBulkStages;
+      const long long refill = k - 1 + stages;
       if (k >= 1 && refill < mine) {
         bulk_wait_read<1>();
-        const int rs = static_cast<int>((k - 1) % kBulkStages);
+        const int rs = static_cast<int>((k - 1) % stages);
         size_t roff;
         uint32_t rsize;
         bulk_chunk(body, refill, &roff, &rsize);
@@ -231,7 +232,10 @@ __global__ void __launch_bounds__(1024)
 
 }  // namespace
 
-int copy_bulk_smem_bytes() { return kBulkStages * kBulkChunk; }
+int copy_bulk_stages(int requested) {
+  return requested == 0 ? kBulkDefaultStages : requested;
+}
+int copy_bulk_smem_bytes(int stages) { return stages * kBulkChunk; }
 
 }  // namespace tcb
 
@@ -262,20 +266,21 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
                                                   static_cast<uint4*>(dst), bytes);
     return launch_status();
   }
-  // Bulk-copy engine: one warp per CTA (lane 0 drives the ring).
-  if (threads != 0 && threads != 32) return TCB_ERR_INVALID_ARGUMENT;
-  const int smem = copy_bulk_smem_bytes();
-  if (smem > facts.max_smem_optin) return TCB_ERR_RESOURCE;
-  static int configured_device = -1;
-  if (configured_device != facts.device) {
-    const int cap =
-        raise_dynamic_smem(reinterpret_cast<const void*>(copy_bulk_kernel), facts.max_smem_optin);
-    if (cap < smem) return TCB_ERR_RESOURCE;
-    configured_device = facts.device;
+  // Bulk-copy engine: one warp per CTA (lane 0 drives the ring); `threads`
+  // selects the ring depth in 32 KiB chunks.
+  const int stages = copy_bulk_stages(threads);
+  if (stages < 2 || stages > kBulkMaxStages) return TCB_ERR_INVALID_ARGUMENT;
+  const int smem = copy_bulk_smem_bytes(stages);
+  static int cap_device = -1, cap = 0;
+  if (cap_device != facts.device) {
+    cap = raise_dynamic_smem(reinterpret_cast<const void*>(copy_bulk_kernel), facts.max_smem_optin);
+    cap_device = facts.device;
   }
-  if (blocks == 0) blocks = facts.sm_count;
+  if (cap < smem) return TCB_ERR_RESOURCE;
+  if (blocks == 0) blocks = facts.sm_count * 4;
   copy_bulk_kernel<<<blocks, 32, smem, s>>>(static_cast<const unsigned char*>(src),
-                                            static_cast<unsigned char*>(dst), bytes, nullptr);
+                                            static_cast<unsigned char*>(dst), bytes, stages,
+                                            nullptr);
   return launch_status();
 }
 
@@ -318,7 +323,8 @@ int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out) {
                                             : reinterpret_cast<const void*>(copy_ldg128_kernel);
   if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
-  out->dynamic_smem_bytes = variant == TCB_COPY_BULK ? copy_bulk_smem_bytes() : 0;
+  out->dynamic_smem_bytes =
+      variant == TCB_COPY_BULK ? copy_bulk_smem_bytes(copy_bulk_stages(threads)) : 0;
   out->threads_per_block = variant == TCB_COPY_BULK ? 32 : (threads ? threads : 512);
   out->tensor_core = 0;
   copy_str(out->instruction, sizeof(out->instruction),
