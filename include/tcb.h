@@ -77,7 +77,7 @@ int tcb_device_query(int device, tcb_device_props *out);
  * loop.  blocks = 0 selects the tuned grid for the variant.  For LDG128,
  * `threads` is the CTA size (0: 512).  For BULK the CTA is one warp and
  * `threads` is the depth of the shared-memory ring in 32 KiB chunks (2..8,
- * 0: 4). src and dst must not overlap.
+ * 0: 2; the default grid is 2 CTAs per SM). src and dst must not overlap.
  * Replaces launch_copy (bench_bandwidth.py:43-47) and copy_kernel
  * (bench_bandwidth.py:36-40). */
 int tcb_copy(const void *src, void *dst, size_t bytes, int variant, int blocks, int threads,

@@ -26,7 +26,7 @@ namespace {
 constexpr int kCopyUnroll = 4;
 constexpr int kBulkChunk = 32768;
 constexpr int kBulkMaxStages = 8;
-constexpr int kBulkDefaultStages = 4;
+constexpr int kBulkDefaultStages = 2;
 
 __device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) {
   uint4 v;
@@ -277,7 +277,7 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
     cap_device = facts.device;
   }
   if (cap < smem) return TCB_ERR_RESOURCE;
-  if (blocks == 0) blocks = facts.sm_count * 4;
+  if (blocks == 0) blocks = facts.sm_count * 2;
   copy_bulk_kernel<<<blocks, 32, smem, s>>>(static_cast<const unsigned char*>(src),
                                             static_cast<unsigned char*>(dst), bytes, stages,
                                             nullptr);
