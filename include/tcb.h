@@ -144,6 +144,19 @@ int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const 
                     int tile_n, int tile_k, int chains, int iterations, int *status_dev,
                     tcb_stream_t stream);
 
+/* ------------------------------------------------------------- GEMM */
+/* C[M][N] = A[M][K] . B[N][K]^T with A and B K-contiguous, C row-major fp32
+ * (int32 for TCB_T_INT8).  dtype: TCB_T_BF16, FP16, TF32, INT8, FP8E4M3, MXF4.
+ * For MXF4, A and B hold E2M1 codes packed two per byte along K (low nibble =
+ * even k) and SA [M][K/32], SB [N][K/32] hold E8M0 scales (8-byte aligned).
+ * Constraints: M % 128 == 0, N % 256 == 0, K x element bits % 1024 == 0 (whole
+ * 128-byte K blocks); otherwise TCB_ERR_UNSUPPORTED.  blocks = 0 selects one
+ * persistent CTA per SM.  Replaces run_gemm / _gemm_kernel
+ * (bench_tensor.py:172-209, 1509-1595); the MX FP4 GEMM has no counterpart in
+ * the reference (which refuses FP4 GEMM, bench_tensor.py:1406-1407). */
+int tcb_gemm(int dtype, const void *A, const void *B, const void *SA, const void *SB, void *C,
+             int M, int N, int K, int blocks, int *status_dev, tcb_stream_t stream);
+
 /* ------------------------------------------------------- kernel info */
 #define TCB_FAMILY_COPY 0
 #define TCB_FAMILY_READ 1
@@ -169,6 +182,7 @@ typedef struct tcb_kernel_info_t {
  *   READ   : dtype, threads
  *   VECTOR : dtype, threads, elems_per_thread, unroll
  *   TENSOR : dtype, variant, tile_m, tile_n, tile_k, chains (blocks_per_sm via a6)
+ *   GEMM_FP4 (any GEMM dtype): dtype
  * Replaces the CompiledKernel metadata read by _compiled_info
  * (bench_tensor.py:984-1146) and inspect_assembly (bench_vector.py:623-799). */
 int tcb_kernel_info(int family, int a0, int a1, int a2, int a3, int a4, int a5, int a6,

@@ -181,3 +181,54 @@ def test_kernel_info_reports_instruction(native, cuda):
     assert info["local_bytes_per_thread"] == 0
     simt = native.kernel_info(native.FAMILY_TENSOR, FP32, SIMT, 256, 256, 32, 1, 1)
     assert simt["instruction"] == "fma.rn.f32" and simt["execution_kind"] == "simt"
+
+
+GEMM_CASES = [(BF16, 256, 256, 64), (BF16, 512, 512, 1024), (FP16, 384, 512, 192),
+              (TF32, 256, 256, 96), (INT8, 256, 512, 256), (FP8, 256, 256, 512),
+              (MXF4, 256, 256, 256), (MXF4, 512, 768, 2048), (MXF4, 128, 256, 8192)]
+
+
+@pytest.mark.parametrize("dtype,m,n,k", GEMM_CASES)
+def test_gemm_exact(cuda, native, dtype, m, n, k):
+    """C = A . B^T through tcb_gemm against the exact host product."""
+    a, b = _operands(dtype, 1, 1, m, n, k, seed=m + n + k)
+    a, b = a[0], b[0, 0]
+    sa = sb = None
+    if dtype == MXF4:
+        gen = torch.Generator().manual_seed(k)
+        sa = torch.randint(125, 130, (m, k // 32), generator=gen, dtype=torch.uint8)
+        sb = torch.randint(125, 130, (n, k // 32), generator=gen, dtype=torch.uint8)
+    out_dtype = torch.int32 if dtype == INT8 else torch.float32
+    c = torch.full((m, n), -7, dtype=out_dtype, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    native.gemm(dtype, a.to(cuda), b.to(cuda), c, m, n, k,
+                scale_a=None if sa is None else sa.to(cuda),
+                scale_b=None if sb is None else sb.to(cuda), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    if dtype == MXF4:
+        ref = oracle_tensor.resident_reference(a.numpy(), b.numpy(), 1, "fp4", sa.numpy(),
+                                               sb.numpy())
+    else:
+        ref = oracle_tensor.resident_reference(_host(a), _host(b), 1, NAME[dtype])
+    assert np.array_equal(c.cpu().double().numpy(), ref.astype(np.float64))
+
+
+def test_gemm_persistent_tiles(cuda, native):
+    """More tiles than CTAs: each CTA walks several tiles through one accumulator."""
+    m, n, k = 1024, 1024, 512
+    a, b = _operands(BF16, 1, 1, m, n, k, seed=3)
+    a, b = a[0], b[0, 0]
+    c = torch.zeros((m, n), device=cuda)
+    native.gemm(BF16, a.to(cuda), b.to(cuda), c, m, n, k, blocks=5)
+    torch.cuda.synchronize()
+    ref = oracle_tensor.resident_reference(_host(a), _host(b), 1, "bf16")
+    assert np.array_equal(c.cpu().double().numpy(), ref)
+
+
+def test_gemm_rejects_unsupported_shapes(cuda, native):
+    a = torch.zeros((128, 64), dtype=torch.bfloat16, device=cuda)
+    c = torch.zeros((128, 128), device=cuda)
+    with pytest.raises(native.TcbError) as info:
+        native.gemm(BF16, a, a[:128], c, 128, 128, 64)
+    assert info.value.is_capability

@@ -33,12 +33,12 @@ V_BF16, V_FP16, V_FP32, V_FP64, V_INT8_DP4A, V_INT32_IMAD, V_INT8_MULADD = range
 T_BF16, T_FP16, T_TF32, T_FP32, T_FP64, T_INT8, T_FP8E4M3, T_MXF4 = range(8)
 TV_TCGEN05, TV_DMMA, TV_SIMT = 0, 1, 2
 
-FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR = 0, 1, 2, 3
+FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR, FAMILY_GEMM = 0, 1, 2, 3, 4
 
 # Every symbol include/tcb.h declares.
 EXPORTED_SYMBOLS = (
     "tcb_strerror", "tcb_version", "tcb_device_query", "tcb_copy", "tcb_read",
-    "tcb_vector_chains", "tcb_tensor_peak", "tcb_kernel_info",
+    "tcb_vector_chains", "tcb_tensor_peak", "tcb_gemm", "tcb_kernel_info",
 )
 
 
@@ -128,6 +128,7 @@ def load() -> ctypes.CDLL:
         lib.tcb_read.argtypes = [vp, i, ll, vp, i, i, vp]
         lib.tcb_vector_chains.argtypes = [i, vp, vp, vp, ll, i, i, i, i, i, vp]
         lib.tcb_tensor_peak.argtypes = [i, i, vp, vp, vp, vp, vp, i, i, i, i, i, i, i, vp, vp]
+        lib.tcb_gemm.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_kernel_info.argtypes = [i, i, i, i, i, i, i, i, ctypes.POINTER(KernelInfo)]
         for name in EXPORTED_SYMBOLS:
             if name not in ("tcb_strerror", "tcb_version"):
@@ -223,6 +224,12 @@ def tensor_peak(dtype: int, variant: int, a, b, c, *, blocks: int, blocks_per_sm
     check(load().tcb_tensor_peak(dtype, variant, _ptr(a), _ptr(b), _ptr(scale_a), _ptr(scale_b),
                                  _ptr(c), blocks, blocks_per_sm, tile_m, tile_n, tile_k, chains,
                                  iterations, _ptr(status), _stream(stream)), "tcb_tensor_peak")
+
+
+def gemm(dtype: int, a, b, c, m: int, n: int, k: int, *, scale_a=None, scale_b=None,
+         blocks: int = 0, status=None, stream=None) -> None:
+    check(load().tcb_gemm(dtype, _ptr(a), _ptr(b), _ptr(scale_a), _ptr(scale_b), _ptr(c), m, n, k,
+                          blocks, _ptr(status), _stream(stream)), "tcb_gemm")
 
 
 def kernel_info(family: int, *args: int) -> dict:

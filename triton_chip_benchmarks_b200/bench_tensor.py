@@ -505,6 +505,124 @@ def emit_tensor_results(metadata, args, rows) -> None:
         emit_results("tensor", metadata, args, rows)
 
 
+# ---------------------------------------------------------------- GEMM mode
+GEMM_KEYS = ("bf16", "fp16", "tf32", "int8", "fp8", "fp4")
+GEMM_TOLERANCE = {"bf16": 2e-3, "fp16": 2e-3, "tf32": 1e-2, "int8": 0.0, "fp8": 0.0, "fp4": 0.0}
+
+
+def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
+    """A [M,K], B [N,K] (K contiguous), scales for MX FP4, and the FP32 operand values.
+
+    bf16/fp16/tf32 follow the reference's GEMM inputs (bench_tensor.py:249-261):
+    normal A, normal B scaled by 1/sqrt(K); int8 is ternary; fp8 uses integers in
+    [-3, 3]/4 and fp4 draws all 16 E2M1 codes with unit scales, so those two are
+    exact in FP32.
+    """
+    if key == "fp4":
+        a_codes = torch.randint(0, 16, (m, k), generator=gen, dtype=torch.uint8)
+        b_codes = torch.randint(0, 16, (n, k), generator=gen, dtype=torch.uint8)
+        a = pack_e2m1_pairs(a_codes).to(device)
+        b = pack_e2m1_pairs(b_codes).to(device)
+        sa = torch.full((m, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
+        sb = torch.full((n, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
+        return a, b, (sa, sb)
+    if key == "int8":
+        return (torch.randint(-1, 2, (m, k), generator=gen).to(torch.int8).to(device),
+                torch.randint(-1, 2, (n, k), generator=gen).to(torch.int8).to(device), None)
+    if key == "fp8":
+        return ((torch.randint(-3, 4, (m, k), generator=gen).double() / 4)
+                .to(torch.float8_e4m3fn).to(device),
+                (torch.randint(-3, 4, (n, k), generator=gen).double() / 4)
+                .to(torch.float8_e4m3fn).to(device), None)
+    dtype = STORAGE[key]
+    a = torch.randn((m, k), generator=gen).to(dtype).to(device)
+    b = (torch.randn((n, k), generator=gen) * (1.0 / math.sqrt(k))).to(dtype).to(device)
+    return a, b, None
+
+
+def gemm_reference(key: str, a, b) -> torch.Tensor:
+    """FP32 (INT32) reference product on the device, full precision (no TF32)."""
+    previous = torch.backends.cuda.matmul.fp32_precision
+    torch.backends.cuda.matmul.fp32_precision = "ieee"
+    try:
+        if key == "fp4":
+            av, bv = decode_e2m1(a).float(), decode_e2m1(b).float()
+        else:
+            av, bv = a.float(), b.float()
+        out = torch.matmul(av, bv.t())
+    finally:
+        torch.backends.cuda.matmul.fp32_precision = previous
+    return out.to(torch.int32) if key == "int8" else out
+
+
+def run_gemm(args, metadata) -> None:
+    key = math_key(args)
+    device = torch.device("cuda", args.device)
+    sizes = args.sizes
+    unit = "TOPS" if key == "int8" else "TFLOP/s"
+    print(f"\nMatrix GEMM: {key} inputs, {accumulator_name(key).upper()} accumulate/output; "
+          "2*M*N*K operations; tcgen05 persistent 128x256 tiles")
+    print("     N  median ms  min ms  median " + unit + "  peak " + unit + "  max abs error")
+    info = _native.kernel_info(_native.FAMILY_GEMM, NATIVE[key])
+    audit = compiled_info(key, info, True)
+    rows = []
+    gen = torch.Generator().manual_seed(args.seed)
+    for size in sizes:
+        m = n = k = size
+        base = {"mode": "gemm", "m": m, "n": n, "k": k, "dtype": key}
+        need = size * size * (64 if key != "fp4" else 16)
+        free = available_memory_bytes()
+        if free is not None and need > free * 0.8:
+            raise RuntimeError(f"N={size} needs about {need / 2**30:.1f} GiB of device memory")
+        a, b, scales = gemm_inputs(key, m, n, k, device, gen)
+        sa, sb = scales if scales is not None else (None, None)
+        c = torch.full((m, n), float("nan") if key != "int8" else 0, device=device,
+                       dtype=torch.int32 if key == "int8" else torch.float32)
+        if key == "int8":
+            c.fill_(-2**31)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+
+        def run():
+            _native.gemm(NATIVE[key], a, b, c, m, n, k, scale_a=sa, scale_b=sb, status=status)
+
+        try:
+            run()
+        except _native.TcbError as exc:
+            if exc.is_capability or exc.is_resource:
+                rows.append({**base, "status": "unsupported" if exc.is_capability else "skipped",
+                             "reason": str(exc)})
+                continue
+            raise
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError(f"device-side wait failed: {_native.strerror(int(status.item()))}")
+        reference = gemm_reference(key, a, b)
+        tol = GEMM_TOLERANCE[key]
+        torch.testing.assert_close(c, reference, rtol=tol, atol=tol)
+        max_err = (c.double() - reference.double()).abs().max().item()
+        correctness = {"passed": True, "max_abs_error": max_err, "rtol": tol, "atol": tol,
+                       "reference": "FP32 torch.matmul of the decoded operands, IEEE precision"
+                       if key != "int8" else "exact ternary product converted to INT32"}
+        del reference
+        timing = measure(run, args)
+        rate = rates(2 * m * n * k, timing, key)
+        row = {**base, "measurement_kind": "dense_tensor_gemm",
+               "execution_kind": audit["execution_kind"],
+               "precision_verified": audit["instruction_precision_verified"],
+               "accumulator_dtype": accumulator_name(key), "output_dtype": accumulator_name(key),
+               **precision_descriptor(args.dtype, args.input_precision), **rate,
+               "config": {"block_m": 128, "block_n": 256, "block_k_bytes": 128, "stages": 4,
+                          "persistent": True},
+               "status": "ok", "correctness": correctness, "compiled": audit, **timing}
+        rows.append(row)
+        print(f"{size:6d} {timing['median_ms']:10.4f} {timing['min_ms']:7.4f} "
+              f"{rate['median_teraops_per_second']:12.2f} {rate['peak_teraops_per_second']:10.2f} "
+              f"{max_err:.3g}", flush=True)
+        del a, b, c, scales
+        torch.cuda.empty_cache()
+    emit_tensor_results(metadata, args, rows)
+
+
 def build_parser():
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--mode", choices=("peak", "gemm"), default="peak",
@@ -545,9 +663,14 @@ def main(argv=None) -> None:
     metadata = setup_device(args)
     metadata.update(precision_descriptor(args.dtype, args.input_precision))
     if args.mode == "gemm":
-        emit_not_implemented("tensor", metadata, args,
-                             "This build implements the resident peak mode; application GEMM "
-                             "mode is not implemented")
+        key = math_key(args)
+        if key not in GEMM_KEYS:
+            emit_not_implemented("tensor", metadata, args,
+                                 f"This build's GEMM mode runs on tcgen05 tensor cores "
+                                 f"({', '.join(sorted(GEMM_KEYS))}); {key} GEMM is not "
+                                 "implemented")
+            return
+        run_gemm(args, metadata)
         return
     if not metadata["architecture"].startswith("sm_10"):
         emit_unsupported("tensor", metadata, args,

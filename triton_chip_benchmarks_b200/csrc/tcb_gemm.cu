@@ -1,0 +1,435 @@
+// Dense GEMM on 5th-generation tensor cores (sm_100a): C = A . B^T.
+//
+// A [M][K] and B [N][K] are K-contiguous ("TN"); C [M][N] is fp32 (int32 for
+// INT8).  MX FP4 operands are E2M1 packed two per byte along K with one E8M0
+// scale per 32 elements along K (SA [M][K/32], SB [N][K/32]).
+//
+// Persistent kernel, one CTA per SM, 128 x 256 output tiles, warp-specialised:
+//   warp 0      TMA producer: per 128-byte K block, A [128 x 128 B] and
+//               B [256 x 128 B] tiles (SWIZZLE_128B) into a ring of STAGES
+//               shared-memory stages, completing on full[stage];
+//   warp 1      MMA issuer: waits full[stage], issues the block's four
+//               tcgen05.mma (M=128, N=256, K=32 B each) into one tensor-memory
+//               accumulator, commits to empty[stage]; after the last block
+//               commits to acc_full;
+//   warps 2-5   epilogue: wait acc_full, tcgen05.ld their 32 lanes x 256
+//               columns, store C, arrive acc_empty;
+//   warps 6-9   (MX FP4 only) scale writers: per K block read the E8M0 pairs of
+//               the tile's rows and write them into a tensor-memory scale ring
+//               (same stage index), then arrive on full[stage].
+// Every wait is bounded; a timeout raises a CTA-wide abort flag so all roles
+// leave their loops, and tensor memory is released at the end.
+//
+// Counterpart in the reference suite: the application GEMM of run_gemm /
+// _gemm_kernel (bench_tensor.py:172-209, 1509-1595); the MX FP4 GEMM has no
+// counterpart there (FP4 GEMM is refused at bench_tensor.py:1406-1407).
+#include <cudaTypedefs.h>
+
+#include "tcb_device.cuh"
+#include "tcb_host.h"
+#include "tcb_registry.h"
+
+namespace tcb {
+namespace {
+
+enum GKind : int { gF16 = 0, gBF16 = 1, gTF32 = 2, gI8 = 3, gE4M3 = 4, gMXF4 = 5 };
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kBlockBytes = 128;     // K bytes per pipeline stage (one SWIZZLE_128B panel)
+constexpr int kStepsPerBlock = 4;    // 32-byte MMA K steps per block
+constexpr int kStages = 4;
+constexpr int kStageA = kTileM * kBlockBytes;   // 16 KB
+constexpr int kStageB = kTileN * kBlockBytes;   // 32 KB
+constexpr int kStageBytes = kStageA + kStageB;  // 48 KB
+constexpr int kAccCols = kTileN;                // fp32 accumulator columns
+constexpr int kSfStepCols = 4 + kTileN / 32;    // A: 4 columns, B: 8 columns per K step
+constexpr int kSfStageCols = kStepsPerBlock * kSfStepCols;
+constexpr int kTmemCols = 512;
+constexpr int kEpilogueWarps = 4;
+constexpr int kScaleWarps = 4;
+
+struct GemmArgs {
+  const uint8_t* sa;  // [M][K/32] E8M0 (MX FP4)
+  const uint8_t* sb;  // [N][K/32]
+  uint32_t* c;        // [M][N] 32-bit
+  int* status;
+  int m, n, kbytes, kgroups;  // kgroups = K/32 scale groups per row
+  int tiles_m, tiles_n, kblocks;
+  uint32_t idesc;
+};
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - start > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      report_status(status, TCB_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ void gemm_mma(uint32_t d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate, uint32_t tsfa,
+                                         uint32_t tsfb) {
+  if constexpr (KIND == gF16 || KIND == gBF16) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (KIND == gTF32) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (KIND == gI8) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (KIND == gE4M3) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, "
+                 "[%5], [%6], p;\n\t}" ::"r"(d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ __align__(8) uint64_t acc_empty;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr bool kScaled = KIND == gMXF4;
+  const int tiles = args.tiles_m * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&map_a);
+    prefetch_tensormap(&map_b);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], kScaled ? 1 + kScaleWarps : 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_init(&acc_empty, kEpilogueWarps);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+        const int tm = t % args.tiles_m, tn = t / args.tiles_m;
+        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
+          if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
+          uint8_t* stage = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(stage, &map_a, kb * kBlockBytes, tm * kTileM, &full[s]);
+          tma_load_2d(stage + kStageA, &map_b, kb * kBlockBytes, tn * kTileN, &full[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      const uint64_t desc_const = smem_desc(0, 16, 8 * kBlockBytes, 2u);
+      const uint32_t smem0 = smem_addr(smem) >> 4;
+      int it = 0, ti = 0;
+      for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++ti) {
+        if (!wait_or_abort(&acc_empty, (static_cast<uint32_t>(ti) & 1u) ^ 1u, &abort_flag,
+                           args.status))
+          break;
+        tc_fence_after();
+        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
+          if (!wait_or_abort(&full[s], phase, &abort_flag, args.status)) break;
+          tc_fence_after();
+          const uint32_t a_lo = smem0 + static_cast<uint32_t>(s * kStageBytes >> 4);
+          const uint32_t b_lo = a_lo + (kStageA >> 4);
+          const uint32_t sf = tbase + kAccCols + static_cast<uint32_t>(s * kSfStageCols);
+#pragma unroll
+          for (int k = 0; k < kStepsPerBlock; ++k) {
+            const uint64_t ad = desc_const | (a_lo + static_cast<uint32_t>(k * 2));
+            const uint64_t bd = desc_const | (b_lo + static_cast<uint32_t>(k * 2));
+            gemm_mma<KIND>(tbase, ad, bd, args.idesc, (kb | k) != 0,
+                           sf + k * kSfStepCols, sf + k * kSfStepCols + 4);
+          }
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + kEpilogueWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    int ti = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
+      if (!wait_or_abort(&acc_full, static_cast<uint32_t>(ti) & 1u, &abort_flag, args.status))
+        break;
+      tc_fence_after();
+      const int tm = t % args.tiles_m, tn = t / args.tiles_m;
+      const int row = tm * kTileM + 32 * quarter + lane;
+      uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
+      const uint32_t taddr = tbase + ((32u * quarter) << 16);
+#pragma unroll 1
+      for (int j = 0; j < kTileN / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld_32cols(taddr + 32 * j, r);
+        tmem_wait_ld();
+        uint4* out = reinterpret_cast<uint4*>(dst + 32 * j);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          out[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty);
+    }
+  } else if (kScaled) {
+    // ------------------------------------------------------ scale writers
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+      const int tm = t % args.tiles_m, tn = t / args.tiles_m;
+      const uint8_t* sa = args.sa + static_cast<size_t>(tm * kTileM + lane) * args.kgroups;
+      const uint8_t* sb = args.sb + static_cast<size_t>(tn * kTileN + lane) * args.kgroups;
+      for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
+        // Eight E8M0 bytes (four 64-element steps x two groups) per row and block.
+        uint2 fa[4], fb[kTileN / 32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          fa[j] = *reinterpret_cast<const uint2*>(sa + static_cast<size_t>(32 * j) * args.kgroups +
+                                                   kb * 8);
+#pragma unroll
+        for (int j = 0; j < kTileN / 32; ++j)
+          fb[j] = *reinterpret_cast<const uint2*>(sb + static_cast<size_t>(32 * j) * args.kgroups +
+                                                   kb * 8);
+        if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
+        const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
+#pragma unroll
+        for (int k = 0; k < kStepsPerBlock; ++k) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t w = k < 2 ? fa[j].x : fa[j].y;
+            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
+            tmem_st_1col(lane_base + col0 + k * kSfStepCols + j, v | (v << 16));
+          }
+#pragma unroll
+          for (int j = 0; j < kTileN / 32; ++j) {
+            const uint32_t w = k < 2 ? fb[j].x : fb[j].y;
+            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
+            tmem_st_1col(lane_base + col0 + k * kSfStepCols + 4 + j, v | (v << 16));
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
+
+GemmFn gemm_fn(int kind) {
+  switch (kind) {
+    case gF16: return gemm_kernel<gF16>;
+    case gBF16: return gemm_kernel<gBF16>;
+    case gTF32: return gemm_kernel<gTF32>;
+    case gI8: return gemm_kernel<gI8>;
+    case gE4M3: return gemm_kernel<gE4M3>;
+    case gMXF4: return gemm_kernel<gMXF4>;
+  }
+  return nullptr;
+}
+
+int gemm_kind(int dtype) {
+  switch (dtype) {
+    case TCB_T_FP16: return gF16;
+    case TCB_T_BF16: return gBF16;
+    case TCB_T_TF32: return gTF32;
+    case TCB_T_INT8: return gI8;
+    case TCB_T_FP8E4M3: return gE4M3;
+    case TCB_T_MXF4: return gMXF4;
+  }
+  return -1;
+}
+
+int gemm_bits(int kind) {
+  switch (kind) {
+    case gF16:
+    case gBF16: return 16;
+    case gTF32: return 32;
+    case gI8:
+    case gE4M3: return 8;
+    case gMXF4: return 4;
+  }
+  return 0;
+}
+
+uint32_t gemm_idesc(int kind) {
+  uint32_t d = static_cast<uint32_t>(kTileN >> 3) << 17 | static_cast<uint32_t>(kTileM >> 4) << 24;
+  if (kind == gMXF4) return d | 1u << 7 | 1u << 10 | 1u << 23;
+  uint32_t c_fmt = 1, ab = 0;
+  if (kind == gBF16) ab = 1;
+  if (kind == gTF32) ab = 2;
+  if (kind == gI8) c_fmt = 2, ab = 1;
+  return d | c_fmt << 4 | ab << 7 | ab << 10;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes,
+             int box_rows) {
+  auto fn = gemm_encode_fn();
+  if (fn == nullptr) return TCB_ERR_DEVICE;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockBytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TCB_OK : TCB_ERR_INVALID_ARGUMENT;
+}
+
+constexpr int kGemmSmem = kStages * kStageBytes + 1024;
+
+}  // namespace
+
+int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
+  const int kind = gemm_kind(dtype);
+  if (kind < 0) return TCB_ERR_UNSUPPORTED;
+  cudaFuncAttributes attr;
+  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind))) != cudaSuccess)
+    return TCB_ERR_DEVICE;
+  fill_kernel_info(attr, out);
+  out->dynamic_smem_bytes = kGemmSmem;
+  out->threads_per_block = (6 + kScaleWarps) * 32;
+  out->tensor_core = 1;
+  copy_str(out->instruction, sizeof(out->instruction),
+           kind == gMXF4 ? "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32"
+           : kind == gTF32 ? "tcgen05.mma.cta_group::1.kind::tf32"
+           : kind == gI8   ? "tcgen05.mma.cta_group::1.kind::i8"
+           : kind == gE4M3 ? "tcgen05.mma.cta_group::1.kind::f8f6f4"
+                           : "tcgen05.mma.cta_group::1.kind::f16");
+  copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
+  return TCB_OK;
+}
+
+}  // namespace tcb
+
+using namespace tcb;
+
+extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA, const void* SB,
+                        void* C, int M, int N, int K, int blocks, int* status_dev,
+                        tcb_stream_t stream) {
+  const int kind = gemm_kind(dtype);
+  if (kind < 0) return TCB_ERR_UNSUPPORTED;
+  if (A == nullptr || B == nullptr || C == nullptr || M <= 0 || N <= 0 || K <= 0 || blocks < 0)
+    return TCB_ERR_INVALID_ARGUMENT;
+  if (M % kTileM || N % kTileN) return TCB_ERR_UNSUPPORTED;
+  const long long kbits = static_cast<long long>(K) * gemm_bits(kind);
+  if (kbits % (8 * kBlockBytes)) return TCB_ERR_UNSUPPORTED;
+  if (kind == gMXF4 && (SA == nullptr || SB == nullptr)) return TCB_ERR_INVALID_ARGUMENT;
+  if (!aligned(A, 16) || !aligned(B, 16) || !aligned(C, 16)) return TCB_ERR_ALIGNMENT;
+  if (kind == gMXF4 && (!aligned(SA, 8) || !aligned(SB, 8))) return TCB_ERR_ALIGNMENT;
+  DeviceFacts facts;
+  int rc = current_device_facts(&facts);
+  if (rc != TCB_OK) return rc;
+  if (facts.major != 10) return TCB_ERR_UNSUPPORTED;
+  const long long kbytes = kbits / 8;
+  CUtensorMap map_a, map_b;
+  if ((rc = gemm_map(&map_a, A, M, kbytes, kTileM)) != TCB_OK) return rc;
+  if ((rc = gemm_map(&map_b, B, N, kbytes, kTileN)) != TCB_OK) return rc;
+  GemmArgs args;
+  args.sa = static_cast<const uint8_t*>(SA);
+  args.sb = static_cast<const uint8_t*>(SB);
+  args.c = static_cast<uint32_t*>(C);
+  args.status = status_dev;
+  args.m = M;
+  args.n = N;
+  args.kbytes = static_cast<int>(kbytes);
+  args.kgroups = K / 32;
+  args.tiles_m = M / kTileM;
+  args.tiles_n = N / kTileN;
+  args.kblocks = static_cast<int>(kbytes / kBlockBytes);
+  args.idesc = gemm_idesc(kind);
+  GemmFn fn = gemm_fn(kind);
+  static int cap[6][64] = {};
+  if (facts.device >= 64) return TCB_ERR_DEVICE;
+  if (cap[kind][facts.device] == 0) {
+    cap[kind][facts.device] =
+        raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+    if (cap[kind][facts.device] < kGemmSmem) {
+      cap[kind][facts.device] = 0;
+      return TCB_ERR_RESOURCE;
+    }
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  if (blocks == 0) blocks = facts.sm_count;
+  if (blocks > tiles) blocks = tiles;
+  clear_stale_error();
+  fn<<<blocks, (6 + kScaleWarps) * 32, kGemmSmem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      map_a, map_b, args);
+  return launch_status();
+}

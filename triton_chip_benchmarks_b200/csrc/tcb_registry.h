@@ -20,6 +20,7 @@ int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out);
 int read_kernel_info(int dtype, int threads, tcb_kernel_info_t* out);
 int vector_kernel_info(int dtype, int threads, int elems_per_thread, int unroll,
                        tcb_kernel_info_t* out);
+int gemm_kernel_info(int dtype, tcb_kernel_info_t* out);
 int tensor_kernel_info(int dtype, int variant, int tile_m, int tile_n, int tile_k, int chains,
                        int blocks_per_sm, tcb_kernel_info_t* out);
 

@@ -43,8 +43,10 @@ __device__ __forceinline__ void fma_rn<double>(double& acc, double a, double b) 
   asm("fma.rn.f64 %0, %1, %2, %0;" : "+d"(acc) : "d"(a), "d"(b));
 }
 
+// FP32 tiles fit two CTAs per SM (128 registers); FP64 tiles need one.
 template <typename T, int K>
-__global__ void __launch_bounds__(kSimtThreads, 1) simt_peak_kernel(const SimtArgs args) {
+__global__ void __launch_bounds__(kSimtThreads, sizeof(T) == 4 ? 2 : 1)
+    simt_peak_kernel(const SimtArgs args) {
   constexpr int VEC = 16 / sizeof(T);  // elements per 16-byte shared load
   constexpr int GROUPS = 8 / VEC;      // column groups per thread
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_peak_kernel(const SimtAr
         for (int it = 0; it < args.iterations; ++it) {
           // A modest unroll keeps the shared loads of one k ahead of the
           // FMAs without hoisting all K steps' operands into registers.
-#pragma unroll(sizeof(T) == 4 ? 4 : 2)
+#pragma unroll 2
           for (int k = 0; k < K; ++k) {
             T av[8], bv[8];
 #pragma unroll
