@@ -354,6 +354,21 @@ int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_b
 
 constexpr int kGemmSmem = kStages * kStageBytes + 1024;
 
+// The arithmetic instruction each kind's kernel writes, in the same wording as
+// the resident probe's table (operand and accumulator types spelled out).
+const char* gemm_instruction(int kind) {
+  switch (kind) {
+    case gF16: return "tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 -> f32)";
+    case gBF16: return "tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> f32)";
+    case gTF32: return "tcgen05.mma.cta_group::1.kind::tf32 (tf32 x tf32 -> f32)";
+    case gI8: return "tcgen05.mma.cta_group::1.kind::i8 (s8 x s8 -> s32)";
+    case gE4M3: return "tcgen05.mma.cta_group::1.kind::f8f6f4 (e4m3 x e4m3 -> f32)";
+    case gMXF4:
+      return "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 (e2m1 x e2m1, ue8m0 -> f32)";
+  }
+  return "";
+}
+
 }  // namespace
 
 int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
@@ -366,12 +381,7 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   out->dynamic_smem_bytes = kGemmSmem;
   out->threads_per_block = (6 + kScaleWarps) * 32;
   out->tensor_core = 1;
-  copy_str(out->instruction, sizeof(out->instruction),
-           kind == gMXF4 ? "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32"
-           : kind == gTF32 ? "tcgen05.mma.cta_group::1.kind::tf32"
-           : kind == gI8   ? "tcgen05.mma.cta_group::1.kind::i8"
-           : kind == gE4M3 ? "tcgen05.mma.cta_group::1.kind::f8f6f4"
-                           : "tcgen05.mma.cta_group::1.kind::f16");
+  copy_str(out->instruction, sizeof(out->instruction), gemm_instruction(kind));
   copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
   return TCB_OK;
 }

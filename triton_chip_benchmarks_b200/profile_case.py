@@ -10,6 +10,7 @@ those launches (CUDA events).
   python -m triton_chip_benchmarks_b200.profile_case copy --mib 1024 --variant bulk
   python -m triton_chip_benchmarks_b200.profile_case tensor --dtype bf16 --tile 256x256x64
   python -m triton_chip_benchmarks_b200.profile_case vector --dtype fp32
+  python -m triton_chip_benchmarks_b200.profile_case gemm --dtype fp4 --size 4096
 """
 
 from __future__ import annotations
@@ -101,6 +102,28 @@ def case_vector(args) -> dict:
             "iterations": args.iterations, "ms_per_launch": ms, "teraops": ops / (ms * 1e9)}
 
 
+def case_gemm(args) -> dict:
+    from .bench_tensor import gemm_inputs, gemm_reference
+    m = n = k = args.size
+    gen = torch.Generator().manual_seed(0)
+    a, b, scales = gemm_inputs(args.dtype, m, n, k, torch.device("cuda"), gen)
+    sa, sb = scales if scales is not None else (None, None)
+    c = torch.empty((m, n), device="cuda",
+                    dtype=torch.int32 if args.dtype == "int8" else torch.float32)
+
+    def run():
+        _native.gemm(NATIVE[args.dtype], a, b, c, m, n, k, scale_a=sa, scale_b=sb)
+
+    run()
+    torch.cuda.synchronize()
+    ref = gemm_reference(args.dtype, a, b)
+    tol = 1e-2 if args.dtype in ("bf16", "fp16", "tf32") else 0.0
+    torch.testing.assert_close(c, ref, rtol=tol, atol=tol)
+    ms = _time(run, args.launches)
+    return {"case": "gemm", "dtype": args.dtype, "size": args.size, "ms_per_launch": ms,
+            "teraops": 2 * m * n * k / (ms * 1e9)}
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__,
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -119,6 +142,10 @@ def main(argv=None):
     p.add_argument("--blocks-per-sm", type=int, default=1)
     p.add_argument("--iterations", type=int, default=4096)
     p.add_argument("--launches", type=int, default=3)
+    p = sub.add_parser("gemm")
+    p.add_argument("--dtype", default="bf16", choices=("bf16", "fp16", "tf32", "int8", "fp8", "fp4"))
+    p.add_argument("--size", type=int, default=4096)
+    p.add_argument("--launches", type=int, default=3)
     p = sub.add_parser("vector")
     p.add_argument("--dtype", default="fp32", choices=("bf16", "fp16", "fp32", "fp64", "int8"))
     p.add_argument("--int8-op", default="dp4a", choices=("dp4a", "imad", "muladd"))
@@ -130,7 +157,8 @@ def main(argv=None):
     p.add_argument("--launches", type=int, default=3)
     args = parser.parse_args(argv)
     torch.cuda.set_device(0)
-    result = {"copy": case_copy, "tensor": case_tensor, "vector": case_vector}[args.case](args)
+    result = {"copy": case_copy, "tensor": case_tensor, "vector": case_vector,
+              "gemm": case_gemm}[args.case](args)
     print(json.dumps(result))
 
 
