@@ -148,7 +148,8 @@ int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const 
 /* C[M][N] = A[M][K] . B[N][K]^T with A and B K-contiguous, C row-major fp32
  * (int32 for TCB_T_INT8).  dtype: TCB_T_BF16, FP16, TF32, INT8, FP8E4M3, MXF4.
  * For MXF4, A and B hold E2M1 codes packed two per byte along K (low nibble =
- * even k) and SA [M][K/32], SB [N][K/32] hold E8M0 scales (8-byte aligned).
+ * even k) and SA, SB hold the E8M0 scales of A [M][K/32] and B [N][K/32] in
+ * the packed layout written by tcb_mx_scales_pack (8-byte aligned).
  * Constraints: M % 128 == 0, N % 256 == 0, K x element bits % 1024 == 0 (whole
  * 128-byte K blocks); otherwise TCB_ERR_UNSUPPORTED.  blocks = 0 selects one
  * persistent CTA per SM.  Replaces run_gemm / _gemm_kernel
@@ -156,6 +157,15 @@ int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const 
  * the reference (which refuses FP4 GEMM, bench_tensor.py:1406-1407). */
 int tcb_gemm(int dtype, const void *A, const void *B, const void *SA, const void *SB, void *C,
              int M, int N, int K, int blocks, int *status_dev, tcb_stream_t stream);
+
+/* Rearrange E8M0 scales src [rows][groups] (row-major, one byte per 32 K
+ * elements) into the layout tcb_gemm reads: for each block of 128 rows and
+ * each 8 groups (256 K elements), 128 rows x 8 bytes contiguous, i.e.
+ * dst[((r/128)*(groups/8) + g/8)*1024 + (r%128)*8 + g%8] = src[r*groups + g].
+ * Same size as src; rows % 128 == 0 and groups % 8 == 0.  Run once per scale
+ * tensor (it is data preparation, not part of the GEMM).  No counterpart in the
+ * reference. */
+int tcb_mx_scales_pack(const void *src, void *dst, int rows, int groups, tcb_stream_t stream);
 
 /* ------------------------------------------------------- kernel info */
 #define TCB_FAMILY_COPY 0

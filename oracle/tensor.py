@@ -45,6 +45,17 @@ def e8m0_value(code: int) -> float:
     return float("nan") if code == 255 else 2.0 ** (int(code) - 127)
 
 
+def pack_mx_scales(scales: np.ndarray) -> np.ndarray:
+    """The GEMM's packed E8M0 layout: per 128 rows and 8 groups, 128 x 8 bytes.
+
+    dst[((r // 128) * (G // 8) + g // 8) * 1024 + (r % 128) * 8 + g % 8] = src[r, g].
+    (A layout of this build, checked against libtcb's pack kernel on the GPU.)
+    """
+    rows, groups = scales.shape
+    out = np.asarray(scales).reshape(rows // 128, 128, groups // 8, 8).transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(out).reshape(rows, groups)
+
+
 def peak_tolerance(dtype: str, block_k: int, iterations: int) -> float:
     if dtype == "int8":
         return 0.0

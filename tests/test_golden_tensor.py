@@ -156,3 +156,13 @@ def test_fp64_probe_verdicts():
         observed = np.zeros((32, 32))
         observed[:, :16] = answers[v["answer"]]
         assert np.array_equal(observed, expected) == v["accepted"], v
+
+
+def test_pack_mx_scales_layout():
+    """Packed scale layout: row r, group g at ((r//128)*(G//8) + g//8)*1024 + (r%128)*8 + g%8."""
+    rows, groups = 256, 16
+    src = np.arange(rows * groups, dtype=np.int64).reshape(rows, groups) % 251
+    packed = oracle_tensor.pack_mx_scales(src.astype(np.uint8)).reshape(-1)
+    for r, g in ((0, 0), (5, 3), (127, 7), (128, 8), (200, 13), (255, 15)):
+        offset = ((r // 128) * (groups // 8) + g // 8) * 1024 + (r % 128) * 8 + g % 8
+        assert packed[offset] == src[r, g] % 256

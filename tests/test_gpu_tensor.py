@@ -201,9 +201,13 @@ def test_gemm_exact(cuda, native, dtype, m, n, k):
     out_dtype = torch.int32 if dtype == INT8 else torch.float32
     c = torch.full((m, n), -7, dtype=out_dtype, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    native.gemm(dtype, a.to(cuda), b.to(cuda), c, m, n, k,
-                scale_a=None if sa is None else sa.to(cuda),
-                scale_b=None if sb is None else sb.to(cuda), status=status)
+    psa = psb = None
+    if dtype == MXF4:
+        psa, psb = torch.empty_like(sa, device=cuda), torch.empty_like(sb, device=cuda)
+        native.mx_scales_pack(sa.to(cuda), psa, m, k // 32)
+        native.mx_scales_pack(sb.to(cuda), psb, n, k // 32)
+    native.gemm(dtype, a.to(cuda), b.to(cuda), c, m, n, k, scale_a=psa, scale_b=psb,
+                status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     if dtype == MXF4:
@@ -232,3 +236,13 @@ def test_gemm_rejects_unsupported_shapes(cuda, native):
     with pytest.raises(native.TcbError) as info:
         native.gemm(BF16, a, a[:128], c, 128, 128, 64)
     assert info.value.is_capability
+
+
+@pytest.mark.parametrize("rows,groups", [(128, 8), (256, 64), (768, 256)])
+def test_mx_scales_pack_matches_oracle(cuda, native, rows, groups):
+    gen = torch.Generator().manual_seed(rows + groups)
+    src = torch.randint(0, 256, (rows, groups), generator=gen, dtype=torch.uint8)
+    dst = torch.zeros((rows, groups), dtype=torch.uint8, device=cuda)
+    native.mx_scales_pack(src.to(cuda), dst, rows, groups)
+    torch.cuda.synchronize()
+    assert np.array_equal(dst.cpu().numpy(), oracle_tensor.pack_mx_scales(src.numpy()))

@@ -525,7 +525,7 @@ def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
         b = pack_e2m1_pairs(b_codes).to(device)
         sa = torch.full((m, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
         sb = torch.full((n, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
-        return a, b, (sa, sb)
+        return a, b, (pack_scales(sa), pack_scales(sb))
     if key == "int8":
         return (torch.randint(-1, 2, (m, k), generator=gen).to(torch.int8).to(device),
                 torch.randint(-1, 2, (n, k), generator=gen).to(torch.int8).to(device), None)
@@ -538,6 +538,13 @@ def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
     a = torch.randn((m, k), generator=gen).to(dtype).to(device)
     b = (torch.randn((n, k), generator=gen) * (1.0 / math.sqrt(k))).to(dtype).to(device)
     return a, b, None
+
+
+def pack_scales(scales: torch.Tensor) -> torch.Tensor:
+    """E8M0 scales [rows][K/32] in the GEMM's packed layout (tcb_mx_scales_pack)."""
+    packed = torch.empty_like(scales)
+    _native.mx_scales_pack(scales, packed, scales.shape[0], scales.shape[1])
+    return packed
 
 
 def gemm_reference(key: str, a, b) -> torch.Tensor:

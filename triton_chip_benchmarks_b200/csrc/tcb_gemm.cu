@@ -15,8 +15,11 @@
 //   warps 2-5   epilogue: wait acc_full, tcgen05.ld their 32 lanes x 256
 //               columns, store C, arrive acc_empty;
 //   warps 6-9   (MX FP4 only) scale writers: per K block read the E8M0 pairs of
-//               the tile's rows and write them into a tensor-memory scale ring
-//               (same stage index), then arrive on full[stage].
+//               the tile's rows (packed layout, coalesced, one block ahead) and
+//               write them into a tensor-memory scale ring (same stage index),
+//               then arrive on full[stage].
+// Tiles are visited in groups of 8 row-blocks so concurrent tiles share
+// operands in L2; C is written with streaming (evict-first) stores.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so all roles
 // leave their loops, and tensor memory is released at the end.
 //
@@ -76,6 +79,28 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Tile t -> (tm, tn) in groups of kGroupM row-blocks: the tiles a wave of
+// persistent CTAs works on at once share few A row-blocks and B column-blocks,
+// so their operands stay in L2.
+constexpr int kGroupM = 8;
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int* tm, int* tn) {
+  const int per_group = kGroupM * tiles_n;
+  const int group = t / per_group;
+  const int first = group * kGroupM;
+  const int rows = min(tiles_m - first, kGroupM);
+  const int r = t - group * per_group;
+  *tm = first + r % rows;
+  *tn = r / rows;
+}
+
+__device__ __forceinline__ void st_stream_u4(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
 }
 
 template <int KIND>
@@ -151,7 +176,8 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     if (lane == 0) {
       int it = 0;
       for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
-        const int tm = t % args.tiles_m, tn = t / args.tiles_m;
+        int tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
         for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
@@ -204,7 +230,8 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
       if (!wait_or_abort(&acc_full, static_cast<uint32_t>(ti) & 1u, &abort_flag, args.status))
         break;
       tc_fence_after();
-      const int tm = t % args.tiles_m, tn = t / args.tiles_m;
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
       const int row = tm * kTileM + 32 * quarter + lane;
       uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
       const uint32_t taddr = tbase + ((32u * quarter) << 16);
@@ -213,10 +240,9 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
         uint32_t r[32];
         tmem_ld_32cols(taddr + 32 * j, r);
         tmem_wait_ld();
-        uint4* out = reinterpret_cast<uint4*>(dst + 32 * j);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          out[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
       }
       tc_fence_before();
       __syncwarp();
@@ -224,26 +250,38 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     }
   } else if (kScaled) {
     // ------------------------------------------------------ scale writers
+    // Scales are in the packed layout of tcb_mx_scales_pack: for each block of
+    // 128 rows and each 256-element K block, 128 rows x 8 E8M0 bytes, so lane l
+    // reads row 32j+l of a row block with one coalesced 8-byte load.  The loads
+    // for the next K block are issued before this block's tensor-memory writes.
     const int quarter = warp & 3;
     const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
+    const size_t rowblock_bytes = static_cast<size_t>(args.kblocks) * 1024;
     int it = 0;
-    for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
-      const int tm = t % args.tiles_m, tn = t / args.tiles_m;
-      const uint8_t* sa = args.sa + static_cast<size_t>(tm * kTileM + lane) * args.kgroups;
-      const uint8_t* sb = args.sb + static_cast<size_t>(tn * kTileN + lane) * args.kgroups;
+    uint2 fa[4], fb[kTileN / 32];
+    auto load = [&](int tm, int tn, int kb) {
+      const uint8_t* a = args.sa + tm * rowblock_bytes + static_cast<size_t>(kb) * 1024 + lane * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) fa[j] = *reinterpret_cast<const uint2*>(a + 256 * j);
+#pragma unroll
+      for (int j = 0; j < kTileN / 32; ++j) {
+        const uint8_t* b = args.sb + (2 * tn + j / 4) * rowblock_bytes +
+                           static_cast<size_t>(kb) * 1024 + lane * 8;
+        fb[j] = *reinterpret_cast<const uint2*>(b + 256 * (j % 4));
+      }
+    };
+    int first = blockIdx.x;
+    if (first < tiles) {
+      int tm, tn;
+      tile_coords(first, args.tiles_m, args.tiles_n, &tm, &tn);
+      load(tm, tn, 0);
+    }
+    for (int t = first; t < tiles && !abort_flag; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
       for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
-        // Eight E8M0 bytes (four 64-element steps x two groups) per row and block.
-        uint2 fa[4], fb[kTileN / 32];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          fa[j] = *reinterpret_cast<const uint2*>(sa + static_cast<size_t>(32 * j) * args.kgroups +
-                                                   kb * 8);
-#pragma unroll
-        for (int j = 0; j < kTileN / 32; ++j)
-          fb[j] = *reinterpret_cast<const uint2*>(sb + static_cast<size_t>(32 * j) * args.kgroups +
-                                                   kb * 8);
         if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
         const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
 #pragma unroll
@@ -260,6 +298,14 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
             const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
             tmem_st_1col(lane_base + col0 + k * kSfStepCols + 4 + j, v | (v << 16));
           }
+        }
+        // Prefetch the next K block's scales (possibly of the next tile).
+        if (kb + 1 < args.kblocks) {
+          load(tm, tn, kb + 1);
+        } else if (t + static_cast<int>(gridDim.x) < tiles) {
+          int nm, nn;
+          tile_coords(t + gridDim.x, args.tiles_m, args.tiles_n, &nm, &nn);
+          load(nm, nn, 0);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -386,9 +432,33 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   return TCB_OK;
 }
 
+// dst[(r/128)][g/8][r%128][g%8] = src[r][g] for E8M0 scales src [rows][groups].
+__global__ void mx_scales_pack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                      int rows, int groups) {
+  const long long total = static_cast<long long>(rows) * groups;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / groups), g = static_cast<int>(i % groups);
+    const long long o = (static_cast<long long>(r / 128) * (groups / 8) + g / 8) * 1024 +
+                        (r % 128) * 8 + (g % 8);
+    dst[o] = src[i];
+  }
+}
+
 }  // namespace tcb
 
 using namespace tcb;
+
+extern "C" int tcb_mx_scales_pack(const void* src, void* dst, int rows, int groups,
+                                  tcb_stream_t stream) {
+  if (src == nullptr || dst == nullptr || rows <= 0 || groups <= 0) return TCB_ERR_INVALID_ARGUMENT;
+  if (rows % 128 || groups % 8) return TCB_ERR_UNSUPPORTED;
+  if (!aligned(dst, 8)) return TCB_ERR_ALIGNMENT;
+  clear_stale_error();
+  mx_scales_pack_kernel<<<256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, groups);
+  return launch_status();
+}
 
 extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA, const void* SB,
                         void* C, int M, int N, int K, int blocks, int* status_dev,
