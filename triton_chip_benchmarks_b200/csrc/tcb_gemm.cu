@@ -4,7 +4,8 @@
 // INT8).  MX FP4 operands are E2M1 packed two per byte along K with one E8M0
 // scale per 32 elements along K (SA [M][K/32], SB [N][K/32]).
 //
-// Persistent kernel, one CTA per SM, 128 x 256 output tiles, warp-specialised:
+// Persistent kernel, one CTA per SM, 256 x 256 output tiles (two M=128
+// accumulators sharing each B tile; 128 x 256 for MX FP4), warp-specialised:
 //   warp 0      TMA producer: per 128-byte K block, A [128 x 128 B] and
 //               B [256 x 128 B] tiles (SWIZZLE_128B) into a ring of STAGES
 //               shared-memory stages, completing on full[stage];
@@ -37,16 +38,28 @@ namespace {
 
 enum GKind : int { gF16 = 0, gBF16 = 1, gTF32 = 2, gI8 = 3, gE4M3 = 4, gMXF4 = 5 };
 
-constexpr int kTileM = 128;
 constexpr int kTileN = 256;
 constexpr int kBlockBytes = 128;     // K bytes per pipeline stage (one SWIZZLE_128B panel)
 constexpr int kStepsPerBlock = 4;    // 32-byte MMA K steps per block
-constexpr int kStages = 4;
-constexpr int kStageA = kTileM * kBlockBytes;   // 16 KB
-constexpr int kStageB = kTileN * kBlockBytes;   // 32 KB
-constexpr int kStageBytes = kStageA + kStageB;  // 48 KB
-constexpr int kAccCols = kTileN;                // fp32 accumulator columns
+constexpr int kAccCols = kTileN;     // fp32 accumulator columns per M=128 half
+constexpr int kSmemBudget = 227 * 1024 - 1024;
+
+// Tile geometry: HALVES M=128 accumulators share each B tile.  A 256 x 256
+// tile (two halves) feeds the tensor cores with 64 KB per 1024 MMA cycles
+// instead of 48 KB per 512 for 128 x 256, i.e. a third less operand traffic
+// per FLOP; it fills all 512 tensor-memory columns, so MX FP4 (whose scales
+// also live in tensor memory) uses one half.
+template <int HALVES>
+struct Tile {
+  static constexpr int kM = 128 * HALVES;
+  static constexpr int kStageA = kM * kBlockBytes;
+  static constexpr int kStageB = kTileN * kBlockBytes;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = kSmemBudget / kStageBytes > 6 ? 6 : kSmemBudget / kStageBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 1024;
+};
 constexpr int kSfStepCols = 4 + kTileN / 32;    // A: 4 columns, B: 8 columns per K step
+constexpr int kMaxStages = 6;
 constexpr int kSfStageCols = kStepsPerBlock * kSfStepCols;
 constexpr int kTmemCols = 512;
 constexpr int kEpilogueWarps = 4;
@@ -131,13 +144,18 @@ __device__ __forceinline__ void gemm_mma(uint32_t d, uint64_t adesc, uint64_t bd
   }
 }
 
-template <int KIND>
+template <int KIND, int HALVES>
 __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+  using T = Tile<HALVES>;
+  constexpr int kStages = T::kStages;
+  constexpr int kStageA = T::kStageA;
+  constexpr int kStageBytes = T::kStageBytes;
+  constexpr int kTileM = T::kM;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages];
-  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ __align__(8) uint64_t acc_full;
   __shared__ __align__(8) uint64_t acc_empty;
   __shared__ uint32_t tmem_slot;
@@ -211,10 +229,15 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
           const uint32_t sf = tbase + kAccCols + static_cast<uint32_t>(s * kSfStageCols);
 #pragma unroll
           for (int k = 0; k < kStepsPerBlock; ++k) {
-            const uint64_t ad = desc_const | (a_lo + static_cast<uint32_t>(k * 2));
             const uint64_t bd = desc_const | (b_lo + static_cast<uint32_t>(k * 2));
-            gemm_mma<KIND>(tbase, ad, bd, args.idesc, (kb | k) != 0,
-                           sf + k * kSfStepCols, sf + k * kSfStepCols + 4);
+#pragma unroll
+            for (int h = 0; h < HALVES; ++h) {
+              // Half h of A starts 128 rows (16 KB) further into the stage.
+              const uint64_t ad =
+                  desc_const | (a_lo + static_cast<uint32_t>(h * (128 * kBlockBytes >> 4) + k * 2));
+              gemm_mma<KIND>(tbase + h * kAccCols, ad, bd, args.idesc, (kb | k) != 0,
+                             sf + k * kSfStepCols, sf + k * kSfStepCols + 4);
+            }
           }
           tc_commit(&empty[s]);
         }
@@ -232,17 +255,21 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
       tc_fence_after();
       int tm, tn;
       tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
-      const int row = tm * kTileM + 32 * quarter + lane;
-      uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
-      const uint32_t taddr = tbase + ((32u * quarter) << 16);
 #pragma unroll 1
-      for (int j = 0; j < kTileN / 32; ++j) {
-        uint32_t r[32];
-        tmem_ld_32cols(taddr + 32 * j, r);
-        tmem_wait_ld();
+      for (int h = 0; h < HALVES; ++h) {
+        const int row = tm * kTileM + 128 * h + 32 * quarter + lane;
+        uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
+        const uint32_t taddr = tbase + ((32u * quarter) << 16) + h * kAccCols;
+#pragma unroll 1
+        for (int j = 0; j < kTileN / 32; ++j) {
+          uint32_t r[32];
+          tmem_ld_32cols(taddr + 32 * j, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          for (int q = 0; q < 8; ++q)
+            st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2],
+                         r[4 * q + 3]);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -286,18 +313,21 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
         const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
 #pragma unroll
         for (int k = 0; k < kStepsPerBlock; ++k) {
+          uint32_t va[4], vb[kTileN / 32];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint32_t w = k < 2 ? fa[j].x : fa[j].y;
             const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            tmem_st_1col(lane_base + col0 + k * kSfStepCols + j, v | (v << 16));
+            va[j] = v | (v << 16);
           }
 #pragma unroll
           for (int j = 0; j < kTileN / 32; ++j) {
             const uint32_t w = k < 2 ? fb[j].x : fb[j].y;
             const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            tmem_st_1col(lane_base + col0 + k * kSfStepCols + 4 + j, v | (v << 16));
+            vb[j] = v | (v << 16);
           }
+          tmem_st_4cols(lane_base + col0 + k * kSfStepCols, va);
+          tmem_st_8cols(lane_base + col0 + k * kSfStepCols + 4, vb);
         }
         // Prefetch the next K block's scales (possibly of the next tile).
         if (kb + 1 < args.kblocks) {
@@ -325,17 +355,33 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
 
 using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
 
-GemmFn gemm_fn(int kind) {
+// MX FP4 uses 128 x 256 tiles (its scales need tensor-memory columns); the
+// other kinds use 256 x 256 when M allows it.
+int gemm_halves(int kind, int m) { return kind != gMXF4 && m % 256 == 0 ? 2 : 1; }
+
+GemmFn gemm_fn(int kind, int halves) {
+  if (halves == 2) {
+    switch (kind) {
+      case gF16: return gemm_kernel<gF16, 2>;
+      case gBF16: return gemm_kernel<gBF16, 2>;
+      case gTF32: return gemm_kernel<gTF32, 2>;
+      case gI8: return gemm_kernel<gI8, 2>;
+      case gE4M3: return gemm_kernel<gE4M3, 2>;
+    }
+    return nullptr;
+  }
   switch (kind) {
-    case gF16: return gemm_kernel<gF16>;
-    case gBF16: return gemm_kernel<gBF16>;
-    case gTF32: return gemm_kernel<gTF32>;
-    case gI8: return gemm_kernel<gI8>;
-    case gE4M3: return gemm_kernel<gE4M3>;
-    case gMXF4: return gemm_kernel<gMXF4>;
+    case gF16: return gemm_kernel<gF16, 1>;
+    case gBF16: return gemm_kernel<gBF16, 1>;
+    case gTF32: return gemm_kernel<gTF32, 1>;
+    case gI8: return gemm_kernel<gI8, 1>;
+    case gE4M3: return gemm_kernel<gE4M3, 1>;
+    case gMXF4: return gemm_kernel<gMXF4, 1>;
   }
   return nullptr;
 }
+
+int gemm_smem(int halves) { return halves == 2 ? Tile<2>::kSmem : Tile<1>::kSmem; }
 
 int gemm_kind(int dtype) {
   switch (dtype) {
@@ -362,7 +408,7 @@ int gemm_bits(int kind) {
 }
 
 uint32_t gemm_idesc(int kind) {
-  uint32_t d = static_cast<uint32_t>(kTileN >> 3) << 17 | static_cast<uint32_t>(kTileM >> 4) << 24;
+  uint32_t d = static_cast<uint32_t>(kTileN >> 3) << 17 | static_cast<uint32_t>(128 >> 4) << 24;
   if (kind == gMXF4) return d | 1u << 7 | 1u << 10 | 1u << 23;
   uint32_t c_fmt = 1, ab = 0;
   if (kind == gBF16) ab = 1;
@@ -398,7 +444,6 @@ int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_b
   return r == CUDA_SUCCESS ? TCB_OK : TCB_ERR_INVALID_ARGUMENT;
 }
 
-constexpr int kGemmSmem = kStages * kStageBytes + 1024;
 
 // The arithmetic instruction each kind's kernel writes, in the same wording as
 // the resident probe's table (operand and accumulator types spelled out).
@@ -420,11 +465,13 @@ const char* gemm_instruction(int kind) {
 int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   const int kind = gemm_kind(dtype);
   if (kind < 0) return TCB_ERR_UNSUPPORTED;
+  const int halves = gemm_halves(kind, 256);
   cudaFuncAttributes attr;
-  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind))) != cudaSuccess)
+  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind, halves))) !=
+      cudaSuccess)
     return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
-  out->dynamic_smem_bytes = kGemmSmem;
+  out->dynamic_smem_bytes = gemm_smem(halves);
   out->threads_per_block = (6 + kScaleWarps) * 32;
   out->tensor_core = 1;
   copy_str(out->instruction, sizeof(out->instruction), gemm_instruction(kind));
@@ -467,7 +514,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   if (kind < 0) return TCB_ERR_UNSUPPORTED;
   if (A == nullptr || B == nullptr || C == nullptr || M <= 0 || N <= 0 || K <= 0 || blocks < 0)
     return TCB_ERR_INVALID_ARGUMENT;
-  if (M % kTileM || N % kTileN) return TCB_ERR_UNSUPPORTED;
+  if (M % 128 || N % kTileN) return TCB_ERR_UNSUPPORTED;
   const long long kbits = static_cast<long long>(K) * gemm_bits(kind);
   if (kbits % (8 * kBlockBytes)) return TCB_ERR_UNSUPPORTED;
   if (kind == gMXF4 && (SA == nullptr || SB == nullptr)) return TCB_ERR_INVALID_ARGUMENT;
@@ -477,9 +524,11 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   int rc = current_device_facts(&facts);
   if (rc != TCB_OK) return rc;
   if (facts.major != 10) return TCB_ERR_UNSUPPORTED;
+  const int halves = gemm_halves(kind, M);
+  const int tile_m = 128 * halves;
   const long long kbytes = kbits / 8;
   CUtensorMap map_a, map_b;
-  if ((rc = gemm_map(&map_a, A, M, kbytes, kTileM)) != TCB_OK) return rc;
+  if ((rc = gemm_map(&map_a, A, M, kbytes, tile_m)) != TCB_OK) return rc;
   if ((rc = gemm_map(&map_b, B, N, kbytes, kTileN)) != TCB_OK) return rc;
   GemmArgs args;
   args.sa = static_cast<const uint8_t*>(SA);
@@ -490,18 +539,19 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   args.n = N;
   args.kbytes = static_cast<int>(kbytes);
   args.kgroups = K / 32;
-  args.tiles_m = M / kTileM;
+  args.tiles_m = M / tile_m;
   args.tiles_n = N / kTileN;
   args.kblocks = static_cast<int>(kbytes / kBlockBytes);
   args.idesc = gemm_idesc(kind);
-  GemmFn fn = gemm_fn(kind);
-  static int cap[6][64] = {};
+  GemmFn fn = gemm_fn(kind, halves);
+  const int smem = gemm_smem(halves);
+  static int cap[6][2][64] = {};
   if (facts.device >= 64) return TCB_ERR_DEVICE;
-  if (cap[kind][facts.device] == 0) {
-    cap[kind][facts.device] =
-        raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
-    if (cap[kind][facts.device] < kGemmSmem) {
-      cap[kind][facts.device] = 0;
+  int& dev_cap = cap[kind][halves - 1][facts.device];
+  if (dev_cap == 0) {
+    dev_cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+    if (dev_cap < smem) {
+      dev_cap = 0;
       return TCB_ERR_RESOURCE;
     }
   }
@@ -509,7 +559,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   if (blocks == 0) blocks = facts.sm_count;
   if (blocks > tiles) blocks = tiles;
   clear_stale_error();
-  fn<<<blocks, (6 + kScaleWarps) * 32, kGemmSmem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  fn<<<blocks, (6 + kScaleWarps) * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       map_a, map_b, args);
   return launch_status();
 }
