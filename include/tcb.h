@@ -149,7 +149,7 @@ int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const 
  * (int32 for TCB_T_INT8).  dtype: TCB_T_BF16, FP16, TF32, INT8, FP8E4M3, MXF4.
  * For MXF4, A and B hold E2M1 codes packed two per byte along K (low nibble =
  * even k) and SA, SB hold the E8M0 scales of A [M][K/32] and B [N][K/32] in
- * the packed layout written by tcb_mx_scales_pack (8-byte aligned).
+ * the packed layout written by tcb_mx_scales_pack (16-byte aligned).
  * Constraints: M % 128 == 0, N % 256 == 0, K x element bits % 1024 == 0 (whole
  * 128-byte K blocks); otherwise TCB_ERR_UNSUPPORTED.  blocks = 0 selects one
  * persistent CTA per SM.  Replaces run_gemm / _gemm_kernel

@@ -8,17 +8,18 @@
 // accumulators sharing each B tile; 128 x 256 for MX FP4), warp-specialised:
 //   warp 0      TMA producer: per 128-byte K block, A [128 x 128 B] and
 //               B [256 x 128 B] tiles (SWIZZLE_128B) into a ring of STAGES
-//               shared-memory stages, completing on full[stage];
-//   warp 1      MMA issuer: waits full[stage], issues the block's four
+//               shared-memory stages, completing on loaded[stage];
+//   warp 1      MMA issuer: waits loaded[stage] (and full[stage] for MX
+//               scales), issues the block's four
 //               tcgen05.mma (M=128, N=256, K=32 B each) into one tensor-memory
 //               accumulator, commits to empty[stage]; after the last block
 //               commits to acc_full;
 //   warps 2-5   epilogue: wait acc_full, tcgen05.ld their 32 lanes x 256
 //               columns, store C, arrive acc_empty;
-//   warps 6-9   (MX FP4 only) scale writers: per K block read the E8M0 pairs of
-//               the tile's rows (packed layout, coalesced, one block ahead) and
-//               write them into a tensor-memory scale ring (same stage index),
-//               then arrive on full[stage].
+//   warps 6-9   (MX FP4 only) scale writers: the producer also brings each
+//               block's packed E8M0 scales into the stage (bulk copies); the
+//               scale warps move them from shared memory into a tensor-memory
+//               scale ring slot (same stage index) and arrive on full[stage].
 // Tiles are visited in groups of 8 row-blocks so concurrent tiles share
 // operands in L2; C is written with streaming (evict-first) stores.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so all roles
@@ -49,12 +50,14 @@ constexpr int kSmemBudget = 227 * 1024 - 1024;
 // instead of 48 KB per 512 for 128 x 256, i.e. a third less operand traffic
 // per FLOP; it fills all 512 tensor-memory columns, so MX FP4 (whose scales
 // also live in tensor memory) uses one half.
-template <int HALVES>
+template <int HALVES, bool SCALED = false>
 struct Tile {
   static constexpr int kM = 128 * HALVES;
   static constexpr int kStageA = kM * kBlockBytes;
   static constexpr int kStageB = kTileN * kBlockBytes;
-  static constexpr int kStageBytes = kStageA + kStageB;
+  // MX FP4: the packed E8M0 scales of the block (A: kM x 8 B, B: 256 x 8 B).
+  static constexpr int kStageS = SCALED ? (kM + kTileN) * 8 : 0;
+  static constexpr int kStageBytes = kStageA + kStageB + kStageS;
   static constexpr int kStages = kSmemBudget / kStageBytes > 6 ? 6 : kSmemBudget / kStageBytes;
   static constexpr int kSmem = kStages * kStageBytes + 1024;
 };
@@ -88,6 +91,16 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
     }
   }
   return true;
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t size,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(smem_dst)),
+      "l"(src), "r"(size), "r"(smem_addr(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -148,13 +161,15 @@ template <int KIND, int HALVES>
 __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
-  using T = Tile<HALVES>;
+  constexpr bool kScaled = KIND == gMXF4;
+  using T = Tile<HALVES, kScaled>;
   constexpr int kStages = T::kStages;
   constexpr int kStageA = T::kStageA;
   constexpr int kStageBytes = T::kStageBytes;
   constexpr int kTileM = T::kM;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t loaded[kMaxStages];  // TMA bytes of the stage landed
+  __shared__ __align__(8) uint64_t full[kMaxStages];    // MX scales written to tensor memory
   __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ __align__(8) uint64_t acc_full;
   __shared__ __align__(8) uint64_t acc_empty;
@@ -165,14 +180,14 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr bool kScaled = KIND == gMXF4;
   const int tiles = args.tiles_m * args.tiles_n;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_b);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kScaled ? 1 + kScaleWarps : 1);
+      mbar_init(&loaded[s], 1);
+      mbar_init(&full[s], kScaleWarps);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full, 1);
@@ -201,9 +216,18 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
           const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
           if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
           uint8_t* stage = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(stage, &map_a, kb * kBlockBytes, tm * kTileM, &full[s]);
-          tma_load_2d(stage + kStageA, &map_b, kb * kBlockBytes, tn * kTileN, &full[s]);
+          mbar_arrive_expect_tx(&loaded[s], kStageBytes);
+          tma_load_2d(stage, &map_a, kb * kBlockBytes, tm * kTileM, &loaded[s]);
+          tma_load_2d(stage + kStageA, &map_b, kb * kBlockBytes, tn * kTileN, &loaded[s]);
+          if constexpr (kScaled) {
+            // Packed scales: one contiguous KiB per 128 rows and K block.
+            const size_t rb_bytes = static_cast<size_t>(args.kblocks) * 1024;
+            uint8_t* ss = stage + kStageA + T::kStageB;
+            bulk_load_1d(ss, args.sa + tm * rb_bytes + kb * 1024, 1024, &loaded[s]);
+            bulk_load_1d(ss + 1024, args.sb + (2 * tn) * rb_bytes + kb * 1024, 1024, &loaded[s]);
+            bulk_load_1d(ss + 2048, args.sb + (2 * tn + 1) * rb_bytes + kb * 1024, 1024,
+                         &loaded[s]);
+          }
         }
       }
     }
@@ -222,7 +246,10 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
         for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
-          if (!wait_or_abort(&full[s], phase, &abort_flag, args.status)) break;
+          if (!wait_or_abort(&loaded[s], phase, &abort_flag, args.status)) break;
+          if constexpr (kScaled) {
+            if (!wait_or_abort(&full[s], phase, &abort_flag, args.status)) break;
+          }
           tc_fence_after();
           const uint32_t a_lo = smem0 + static_cast<uint32_t>(s * kStageBytes >> 4);
           const uint32_t b_lo = a_lo + (kStageA >> 4);
@@ -277,39 +304,24 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     }
   } else if (kScaled) {
     // ------------------------------------------------------ scale writers
-    // Scales are in the packed layout of tcb_mx_scales_pack: for each block of
-    // 128 rows and each 256-element K block, 128 rows x 8 E8M0 bytes, so lane l
-    // reads row 32j+l of a row block with one coalesced 8-byte load.  The loads
-    // for the next K block are issued before this block's tensor-memory writes.
+    // The producer brings each block's packed scales into the stage with the
+    // operands; lane l takes rows 32j+l (8 bytes each) from shared memory and
+    // writes them into the tensor-memory scale ring slot of the same stage.
     const int quarter = warp & 3;
     const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
-    const size_t rowblock_bytes = static_cast<size_t>(args.kblocks) * 1024;
     int it = 0;
-    uint2 fa[4], fb[kTileN / 32];
-    auto load = [&](int tm, int tn, int kb) {
-      const uint8_t* a = args.sa + tm * rowblock_bytes + static_cast<size_t>(kb) * 1024 + lane * 8;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) fa[j] = *reinterpret_cast<const uint2*>(a + 256 * j);
-#pragma unroll
-      for (int j = 0; j < kTileN / 32; ++j) {
-        const uint8_t* b = args.sb + (2 * tn + j / 4) * rowblock_bytes +
-                           static_cast<size_t>(kb) * 1024 + lane * 8;
-        fb[j] = *reinterpret_cast<const uint2*>(b + 256 * (j % 4));
-      }
-    };
-    int first = blockIdx.x;
-    if (first < tiles) {
-      int tm, tn;
-      tile_coords(first, args.tiles_m, args.tiles_n, &tm, &tn);
-      load(tm, tn, 0);
-    }
-    for (int t = first; t < tiles && !abort_flag; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
+    for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
       for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
-        if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
+        if (!wait_or_abort(&loaded[s], phase, &abort_flag, args.status)) break;
+        const uint8_t* ss = smem + s * kStageBytes + kStageA + T::kStageB + lane * 8;
+        uint2 fa[4], fb[kTileN / 32];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) fa[j] = *reinterpret_cast<const uint2*>(ss + 256 * j);
+#pragma unroll
+        for (int j = 0; j < kTileN / 32; ++j)
+          fb[j] = *reinterpret_cast<const uint2*>(ss + 1024 + 256 * j);
         const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
 #pragma unroll
         for (int k = 0; k < kStepsPerBlock; ++k) {
@@ -328,14 +340,6 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
           }
           tmem_st_4cols(lane_base + col0 + k * kSfStepCols, va);
           tmem_st_8cols(lane_base + col0 + k * kSfStepCols + 4, vb);
-        }
-        // Prefetch the next K block's scales (possibly of the next tile).
-        if (kb + 1 < args.kblocks) {
-          load(tm, tn, kb + 1);
-        } else if (t + static_cast<int>(gridDim.x) < tiles) {
-          int nm, nn;
-          tile_coords(t + gridDim.x, args.tiles_m, args.tiles_n, &nm, &nn);
-          load(nm, nn, 0);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -381,7 +385,10 @@ GemmFn gemm_fn(int kind, int halves) {
   return nullptr;
 }
 
-int gemm_smem(int halves) { return halves == 2 ? Tile<2>::kSmem : Tile<1>::kSmem; }
+int gemm_smem(int kind, int halves) {
+  if (kind == gMXF4) return Tile<1, true>::kSmem;
+  return halves == 2 ? Tile<2>::kSmem : Tile<1>::kSmem;
+}
 
 int gemm_kind(int dtype) {
   switch (dtype) {
@@ -471,7 +478,7 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
       cudaSuccess)
     return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
-  out->dynamic_smem_bytes = gemm_smem(halves);
+  out->dynamic_smem_bytes = gemm_smem(kind, halves);
   out->threads_per_block = (6 + kScaleWarps) * 32;
   out->tensor_core = 1;
   copy_str(out->instruction, sizeof(out->instruction), gemm_instruction(kind));
@@ -519,7 +526,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   if (kbits % (8 * kBlockBytes)) return TCB_ERR_UNSUPPORTED;
   if (kind == gMXF4 && (SA == nullptr || SB == nullptr)) return TCB_ERR_INVALID_ARGUMENT;
   if (!aligned(A, 16) || !aligned(B, 16) || !aligned(C, 16)) return TCB_ERR_ALIGNMENT;
-  if (kind == gMXF4 && (!aligned(SA, 8) || !aligned(SB, 8))) return TCB_ERR_ALIGNMENT;
+  if (kind == gMXF4 && (!aligned(SA, 16) || !aligned(SB, 16))) return TCB_ERR_ALIGNMENT;
   DeviceFacts facts;
   int rc = current_device_facts(&facts);
   if (rc != TCB_OK) return rc;
@@ -544,7 +551,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   args.kblocks = static_cast<int>(kbytes / kBlockBytes);
   args.idesc = gemm_idesc(kind);
   GemmFn fn = gemm_fn(kind, halves);
-  const int smem = gemm_smem(halves);
+  const int smem = gemm_smem(kind, halves);
   static int cap[6][2][64] = {};
   if (facts.device >= 64) return TCB_ERR_DEVICE;
   int& dev_cap = cap[kind][halves - 1][facts.device];
