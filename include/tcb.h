@@ -146,25 +146,37 @@ int tcb_tensor_peak(int dtype, int variant, const void *A, const void *B, const 
 
 /* ------------------------------------------------------------- GEMM */
 /* C[M][N] = A[M][K] . B[N][K]^T with A and B K-contiguous, C row-major fp32
- * (int32 for TCB_T_INT8).  dtype: TCB_T_BF16, FP16, TF32, INT8, FP8E4M3, MXF4.
+ * (int32 for TCB_T_INT8, fp64 for TCB_T_FP64).  dtype: TCB_T_BF16, FP16,
+ * TF32, INT8, FP8E4M3, MXF4 on tcgen05; TCB_T_FP32 (IEEE, fma.rn.f32 on the
+ * FMA pipe) and TCB_T_FP64 (mma.sync f64) on CUDA cores, which take any M,
+ * N, K, element-aligned pointers, and ignore `blocks` and `status_dev`.
  * For MXF4, A and B hold E2M1 codes packed two per byte along K (low nibble =
  * even k) and SA, SB hold the E8M0 scales of A [M][K/32] and B [N][K/32] in
  * the packed layout written by tcb_mx_scales_pack (16-byte aligned).
- * Constraints: M % 128 == 0, N % 256 == 0, K x element bits % 1024 == 0 (whole
- * 128-byte K blocks); otherwise TCB_ERR_UNSUPPORTED.  blocks = 0 selects one
- * persistent CTA per SM.  Replaces run_gemm / _gemm_kernel
- * (bench_tensor.py:172-209, 1509-1595); the MX FP4 GEMM has no counterpart in
- * the reference (which refuses FP4 GEMM, bench_tensor.py:1406-1407). */
+ * tcgen05 kinds: any M, N >= 1 (edge tiles are masked, like the reference's
+ * masked tails); K x element bits must be a multiple of 128 (each row of A and B a whole
+ * number of 16-byte units: K % 8 for 16-bit types, % 4 for TF32, % 16 for
+ * 8-bit, % 32 for MXF4), otherwise TCB_ERR_UNSUPPORTED.  A, B 16-byte
+ * aligned, C 4-byte aligned.  blocks = 0 selects one persistent CTA per SM.
+ * Replaces run_gemm / _launch / _gemm_kernel (bench_tensor.py:172-209,
+ * 235-246, 1509-1595); the MX FP4 GEMM has no counterpart in the reference
+ * (which refuses FP4 GEMM, bench_tensor.py:1406-1407). */
 int tcb_gemm(int dtype, const void *A, const void *B, const void *SA, const void *SB, void *C,
              int M, int N, int K, int blocks, int *status_dev, tcb_stream_t stream);
 
+/* Bytes of the packed scale layout for E8M0 scales [rows][groups]:
+ * rows rounded up to a multiple of 256 times groups rounded up to a multiple
+ * of 8.  Returns TCB_ERR_INVALID_ARGUMENT for non-positive sizes. */
+long long tcb_mx_scales_packed_bytes(int rows, int groups);
+
 /* Rearrange E8M0 scales src [rows][groups] (row-major, one byte per 32 K
- * elements) into the layout tcb_gemm reads: for each block of 128 rows and
- * each 8 groups (256 K elements), 128 rows x 8 bytes contiguous, i.e.
- * dst[((r/128)*(groups/8) + g/8)*1024 + (r%128)*8 + g%8] = src[r*groups + g].
- * Same size as src; rows % 128 == 0 and groups % 8 == 0.  Run once per scale
- * tensor (it is data preparation, not part of the GEMM).  No counterpart in the
- * reference. */
+ * elements) into the layout tcb_gemm reads: rows padded to a multiple of 256
+ * and groups to a multiple of 8 with the unit scale 127, then for each block
+ * of 128 rows and each 8 groups (256 K elements) 128 rows x 8 bytes
+ * contiguous: dst[((r/128)*(groups_p/8) + g/8)*1024 + (r%128)*8 + g%8] =
+ * src[r*groups + g].  dst holds tcb_mx_scales_packed_bytes(rows, groups)
+ * bytes, 16-byte aligned.  Run once per scale tensor (data preparation, not
+ * part of the GEMM).  No counterpart in the reference. */
 int tcb_mx_scales_pack(const void *src, void *dst, int rows, int groups, tcb_stream_t stream);
 
 /* ------------------------------------------------------- kernel info */

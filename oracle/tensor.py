@@ -46,14 +46,18 @@ def e8m0_value(code: int) -> float:
 
 
 def pack_mx_scales(scales: np.ndarray) -> np.ndarray:
-    """The GEMM's packed E8M0 layout: per 128 rows and 8 groups, 128 x 8 bytes.
+    """The GEMM's packed E8M0 layout (this build's own format, flat uint8).
 
-    dst[((r // 128) * (G // 8) + g // 8) * 1024 + (r % 128) * 8 + g % 8] = src[r, g].
-    (A layout of this build, checked against libtcb's pack kernel on the GPU.)
+    Rows are padded to a multiple of 256 and groups to a multiple of 8 with the
+    unit scale 127; then out[((r//128)*(groups_p//8) + g//8)*1024 + (r%128)*8 + g%8]
+    = scales[r, g].
     """
     rows, groups = scales.shape
-    out = np.asarray(scales).reshape(rows // 128, 128, groups // 8, 8).transpose(0, 2, 1, 3)
-    return np.ascontiguousarray(out).reshape(rows, groups)
+    rows_p, groups_p = -(-rows // 256) * 256, -(-groups // 8) * 8
+    padded = np.full((rows_p, groups_p), E8M0_UNIT_SCALE, dtype=np.uint8)
+    padded[:rows, :groups] = scales
+    s = padded.reshape(rows_p // 128, 128, groups_p // 8, 8)
+    return np.ascontiguousarray(s.transpose(0, 2, 1, 3)).reshape(-1)
 
 
 def peak_tolerance(dtype: str, block_k: int, iterations: int) -> float:

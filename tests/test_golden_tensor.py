@@ -166,3 +166,14 @@ def test_pack_mx_scales_layout():
     for r, g in ((0, 0), (5, 3), (127, 7), (128, 8), (200, 13), (255, 15)):
         offset = ((r // 128) * (groups // 8) + g // 8) * 1024 + (r % 128) * 8 + g % 8
         assert packed[offset] == src[r, g] % 256
+
+
+def test_pack_mx_scales_padding():
+    """Ragged scales pad to 256 rows x 8 groups with the unit scale."""
+    src = np.full((130, 17), 3, dtype=np.uint8)
+    packed = oracle_tensor.pack_mx_scales(src)
+    assert packed.size == 256 * 24
+    assert np.count_nonzero(packed == 3) == 130 * 17
+    assert np.all(packed[packed != 3] == oracle_tensor.E8M0_UNIT_SCALE)
+    # row 129, group 16 -> block (1, 2): offset ((1*3 + 2)*1024) + 1*8 + 0
+    assert packed[(1 * 3 + 2) * 1024 + 8] == 3 and packed[(1 * 3 + 2) * 1024 + 8 + 1] == 127

@@ -186,9 +186,19 @@ def test_kernel_info_reports_instruction(native, cuda):
 GEMM_CASES = [(BF16, 256, 256, 64), (BF16, 512, 512, 1024), (FP16, 384, 512, 192),
               (TF32, 256, 256, 96), (INT8, 256, 512, 256), (FP8, 256, 256, 512),
               (MXF4, 256, 256, 256), (MXF4, 512, 768, 2048), (MXF4, 128, 256, 8192)]
+# Masked tails: M, N not tile multiples, ragged last K block, N % 4 != 0 (element
+# stores), single row, and a reference-style odd square size.
+GEMM_TAIL_CASES = [(BF16, 200, 300, 320), (BF16, 128, 258, 64), (TF32, 96, 100, 36),
+                   (INT8, 130, 260, 272), (FP8, 1, 17, 48), (MXF4, 136, 264, 544),
+                   (FP16, 1000, 1000, 1000), (MXF4, 129, 257, 96)]
+# CUDA-core GEMMs (IEEE FP32 SIMT, FP64 DMMA): tile multiples, ragged edges, odd K
+# (element loads), K shorter than one slab.
+GEMM_CC_CASES = [(FP32, 256, 256, 64), (FP32, 200, 130, 37), (FP32, 1, 5, 3),
+                 (FP64, 256, 256, 64), (FP64, 130, 200, 37), (FP64, 129, 127, 1000),
+                 (FP32, 640, 384, 1024)]
 
 
-@pytest.mark.parametrize("dtype,m,n,k", GEMM_CASES)
+@pytest.mark.parametrize("dtype,m,n,k", GEMM_CASES + GEMM_TAIL_CASES + GEMM_CC_CASES)
 def test_gemm_exact(cuda, native, dtype, m, n, k):
     """C = A . B^T through tcb_gemm against the exact host product."""
     a, b = _operands(dtype, 1, 1, m, n, k, seed=m + n + k)
@@ -198,12 +208,15 @@ def test_gemm_exact(cuda, native, dtype, m, n, k):
         gen = torch.Generator().manual_seed(k)
         sa = torch.randint(125, 130, (m, k // 32), generator=gen, dtype=torch.uint8)
         sb = torch.randint(125, 130, (n, k // 32), generator=gen, dtype=torch.uint8)
-    out_dtype = torch.int32 if dtype == INT8 else torch.float32
+    out_dtype = torch.int32 if dtype == INT8 else torch.float64 if dtype == FP64 else torch.float32
     c = torch.full((m, n), -7, dtype=out_dtype, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     psa = psb = None
     if dtype == MXF4:
-        psa, psb = torch.empty_like(sa, device=cuda), torch.empty_like(sb, device=cuda)
+        psa = torch.empty(native.mx_scales_packed_bytes(m, k // 32), dtype=torch.uint8,
+                          device=cuda)
+        psb = torch.empty(native.mx_scales_packed_bytes(n, k // 32), dtype=torch.uint8,
+                          device=cuda)
         native.mx_scales_pack(sa.to(cuda), psa, m, k // 32)
         native.mx_scales_pack(sb.to(cuda), psb, n, k // 32)
     native.gemm(dtype, a.to(cuda), b.to(cuda), c, m, n, k, scale_a=psa, scale_b=psb,
@@ -216,6 +229,22 @@ def test_gemm_exact(cuda, native, dtype, m, n, k):
     else:
         ref = oracle_tensor.resident_reference(_host(a), _host(b), 1, NAME[dtype])
     assert np.array_equal(c.cpu().double().numpy(), ref.astype(np.float64))
+
+
+@pytest.mark.parametrize("key", ["fp32", "tf32", "fp64"])
+def test_gemm_precision_probes(cuda, key):
+    """The reference's fp32/tf32/fp64 probes through the GEMM kernels (gemm mode)."""
+    from triton_chip_benchmarks_b200 import bench_tensor
+    result = bench_tensor.validate_gemm_precision(cuda, key)
+    assert result["passed"] and result["kernel_mode"] == "gemm"
+
+
+def test_gemm_cuda_core_kernel_info(native, cuda):
+    fp32 = native.kernel_info(native.FAMILY_GEMM, FP32)
+    assert fp32["instruction"] == "fma.rn.f32" and fp32["execution_kind"] == "simt"
+    fp64 = native.kernel_info(native.FAMILY_GEMM, FP64)
+    assert "m16n8k4" in fp64["instruction"] and fp64["execution_kind"] == "tensor"
+    assert fp32["local_bytes_per_thread"] == 0 and fp64["local_bytes_per_thread"] == 0
 
 
 def test_gemm_persistent_tiles(cuda, native):
@@ -231,18 +260,20 @@ def test_gemm_persistent_tiles(cuda, native):
 
 
 def test_gemm_rejects_unsupported_shapes(cuda, native):
-    a = torch.zeros((128, 64), dtype=torch.bfloat16, device=cuda)
+    # K = 60 bf16 elements: a 120-byte row is not a whole number of 16-byte units.
+    a = torch.zeros((128, 60), dtype=torch.bfloat16, device=cuda)
     c = torch.zeros((128, 128), device=cuda)
     with pytest.raises(native.TcbError) as info:
-        native.gemm(BF16, a, a[:128], c, 128, 128, 64)
+        native.gemm(BF16, a, a, c, 128, 128, 60)
     assert info.value.is_capability
 
 
-@pytest.mark.parametrize("rows,groups", [(128, 8), (256, 64), (768, 256)])
+@pytest.mark.parametrize("rows,groups", [(128, 8), (256, 64), (768, 256), (130, 17), (1, 1)])
 def test_mx_scales_pack_matches_oracle(cuda, native, rows, groups):
     gen = torch.Generator().manual_seed(rows + groups)
     src = torch.randint(0, 256, (rows, groups), generator=gen, dtype=torch.uint8)
-    dst = torch.zeros((rows, groups), dtype=torch.uint8, device=cuda)
+    dst = torch.zeros(native.mx_scales_packed_bytes(rows, groups), dtype=torch.uint8,
+                      device=cuda)
     native.mx_scales_pack(src.to(cuda), dst, rows, groups)
     torch.cuda.synchronize()
     assert np.array_equal(dst.cpu().numpy(), oracle_tensor.pack_mx_scales(src.numpy()))

@@ -66,3 +66,14 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     with pytest.raises(_native.NativeLibraryError):
         _native.load()
     monkeypatch.delenv("TCB_LIBRARY")
+
+
+def test_mx_scales_packed_bytes_matches_oracle(native):
+    """Host-side size of the packed scale layout (no GPU call)."""
+    import numpy as np
+    from oracle import tensor as oracle_tensor
+    for rows, groups in ((1, 1), (128, 8), (130, 17), (256, 256), (8192, 256)):
+        expected = oracle_tensor.pack_mx_scales(np.zeros((rows, groups), np.uint8)).size
+        assert native.mx_scales_packed_bytes(rows, groups) == expected
+    with pytest.raises(native.TcbError):
+        native.mx_scales_packed_bytes(0, 8)

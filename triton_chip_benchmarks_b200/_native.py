@@ -38,7 +38,8 @@ FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR, FAMILY_GEMM = 0, 1, 2, 3
 # Every symbol include/tcb.h declares.
 EXPORTED_SYMBOLS = (
     "tcb_strerror", "tcb_version", "tcb_device_query", "tcb_copy", "tcb_read",
-    "tcb_vector_chains", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_pack", "tcb_kernel_info",
+    "tcb_vector_chains", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_packed_bytes",
+    "tcb_mx_scales_pack", "tcb_kernel_info",
 )
 
 
@@ -130,10 +131,12 @@ def load() -> ctypes.CDLL:
         lib.tcb_tensor_peak.argtypes = [i, i, vp, vp, vp, vp, vp, i, i, i, i, i, i, i, vp, vp]
         lib.tcb_gemm.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_mx_scales_pack.argtypes = [vp, vp, i, i, vp]
+        lib.tcb_mx_scales_packed_bytes.argtypes = [i, i]
         lib.tcb_kernel_info.argtypes = [i, i, i, i, i, i, i, i, ctypes.POINTER(KernelInfo)]
         for name in EXPORTED_SYMBOLS:
             if name not in ("tcb_strerror", "tcb_version"):
                 getattr(lib, name).restype = i
+        lib.tcb_mx_scales_packed_bytes.restype = ctypes.c_longlong
         _lib = lib
         return lib
 
@@ -231,6 +234,13 @@ def gemm(dtype: int, a, b, c, m: int, n: int, k: int, *, scale_a=None, scale_b=N
          blocks: int = 0, status=None, stream=None) -> None:
     check(load().tcb_gemm(dtype, _ptr(a), _ptr(b), _ptr(scale_a), _ptr(scale_b), _ptr(c), m, n, k,
                           blocks, _ptr(status), _stream(stream)), "tcb_gemm")
+
+
+def mx_scales_packed_bytes(rows: int, groups: int) -> int:
+    """Bytes of the packed E8M0 layout for scales [rows][groups]."""
+    n = load().tcb_mx_scales_packed_bytes(rows, groups)
+    check(n if n < 0 else OK, "tcb_mx_scales_packed_bytes")
+    return int(n)
 
 
 def mx_scales_pack(src, dst, rows: int, groups: int, stream=None) -> None:

@@ -282,6 +282,51 @@ def validate_fp64_precision(device, variant: int) -> dict:
                            "fallback and permuted output rows"}
 
 
+def validate_gemm_precision(device, key: str) -> dict:
+    """The fp32/tf32 and fp64 precision probes through the GEMM kernel itself.
+
+    The reference runs the same probes on its GEMM kernel in --mode gemm
+    (bench_tensor.py:675-714, 717-757 with mode "gemm"): 32 x 32 x 32, B the
+    identity.  fp32/tf32: A holds 1+2**-12 with markers 1+2**-9 and 2**20 in
+    row 0; fp64: A holds 1+2**-40 with a per-row marker in column 0.
+    """
+    size = 32
+    if key == "fp64":
+        a = torch.full((size, size), 1.0 + 2.0**-40, dtype=torch.float64, device=device)
+        a[:, 0] = torch.arange(1, size + 1, dtype=torch.float64, device=device)
+        expected = a.clone()
+        values = [1.0 + 2.0**-40]
+    else:
+        tail, mantissa, exponent = 1.0 + 2.0**-12, 1.0 + 2.0**-9, 2.0**20
+        a = torch.full((size, size), tail, dtype=torch.float32, device=device)
+        a[0, 1], a[0, 2] = mantissa, exponent
+        expected = a.clone()
+        if key == "tf32":
+            expected.fill_(1.0)
+            expected[0, 1], expected[0, 2] = mantissa, exponent
+        values = [tail, mantissa, exponent]
+    b = torch.eye(size, dtype=a.dtype, device=device)
+    c = torch.full((size, size), float("nan"), dtype=a.dtype, device=device)
+    _native.gemm(NATIVE[key], a, b, c, size, size, size)
+    torch.cuda.synchronize(device)
+    error = (c - expected).abs().max().item()
+    if error != 0.0 or not torch.isfinite(c).all():
+        if key == "fp64":
+            permuted = sorted(map(tuple, c.cpu().tolist())) == sorted(map(tuple, expected.cpu().tolist()))
+            raise TensorUnsupportedError(
+                "FP64 GEMM is not exact: " + ("the returned rows are a permutation of the "
+                                              "correct rows" if permuted else f"probe error={error}"))
+        raise TensorUnsupportedError(
+            f"The GEMM did not honour input precision {key!r}: probe expected "
+            f"{expected[0, 0].item()}, observed {c[0, 0].item()}, max error {error}")
+    description = ("FP64 (1+2^-40) with a per-row marker times identity; rejects FP32 fallback "
+                   "and permuted output rows" if key == "fp64" else
+                   "A contains 1+2^-12, 1+2^-9 and 2^20; B=identity; distinguishes IEEE, TF32, "
+                   "BF16 and FP16")
+    return {"passed": True, "max_abs_error": error, "probe_values": values,
+            "kernel_mode": "gemm", "description": description}
+
+
 def validate_fp8_storage(device) -> dict:
     probe = torch.tensor([1 / 16, -1 / 16, 1.0], dtype=torch.float32, device=device)
     restored = probe.to(torch.float8_e4m3fn).float()
@@ -506,8 +551,18 @@ def emit_tensor_results(metadata, args, rows) -> None:
 
 
 # ---------------------------------------------------------------- GEMM mode
-GEMM_KEYS = ("bf16", "fp16", "tf32", "int8", "fp8", "fp4")
-GEMM_TOLERANCE = {"bf16": 2e-3, "fp16": 2e-3, "tf32": 1e-2, "int8": 0.0, "fp8": 0.0, "fp4": 0.0}
+GEMM_KEYS = ("bf16", "fp16", "tf32", "fp32", "fp64", "int8", "fp8", "fp4")
+# The reference's GEMM tolerances (bench_tensor.py:289-299); the formats it does
+# not run in GEMM mode (fp8, fp4) use exact operands.
+GEMM_TOLERANCE = {"bf16": 2e-3, "fp16": 2e-3, "tf32": 1e-2, "fp32": 2e-3, "fp64": 1e-10,
+                  "int8": 0.0, "fp8": 0.0, "fp4": 0.0}
+# Kernel shape reported in each GEMM row.
+GEMM_CONFIG = {
+    "fp32": {"block_m": 128, "block_n": 128, "block_k": 8, "stages": 2, "threads": 256,
+             "kernel": "simt fma.rn.f32, 8x8 register tile"},
+    "fp64": {"block_m": 128, "block_n": 128, "block_k": 16, "stages": 3, "threads": 256,
+             "kernel": "mma.sync m16n8k4 f64, cp.async ring"},
+}
 
 
 def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
@@ -535,20 +590,25 @@ def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
                 (torch.randint(-3, 4, (n, k), generator=gen).double() / 4)
                 .to(torch.float8_e4m3fn).to(device), None)
     dtype = STORAGE[key]
-    a = torch.randn((m, k), generator=gen).to(dtype).to(device)
-    b = (torch.randn((n, k), generator=gen) * (1.0 / math.sqrt(k))).to(dtype).to(device)
+    gen_dtype = torch.float64 if key == "fp64" else torch.float32
+    a = torch.randn((m, k), generator=gen, dtype=gen_dtype).to(dtype).to(device)
+    b = (torch.randn((n, k), generator=gen, dtype=gen_dtype) * (1.0 / math.sqrt(k))) \
+        .to(dtype).to(device)
     return a, b, None
 
 
 def pack_scales(scales: torch.Tensor) -> torch.Tensor:
     """E8M0 scales [rows][K/32] in the GEMM's packed layout (tcb_mx_scales_pack)."""
-    packed = torch.empty_like(scales)
+    packed = torch.empty(_native.mx_scales_packed_bytes(scales.shape[0], scales.shape[1]),
+                         dtype=torch.uint8, device=scales.device)
     _native.mx_scales_pack(scales, packed, scales.shape[0], scales.shape[1])
     return packed
 
 
 def gemm_reference(key: str, a, b) -> torch.Tensor:
-    """FP32 (INT32) reference product on the device, full precision (no TF32)."""
+    """FP32 (INT32, FP64) reference product on the device, full precision (no TF32)."""
+    if key == "fp64":
+        return torch.matmul(a, b.t())
     previous = torch.backends.cuda.matmul.fp32_precision
     torch.backends.cuda.matmul.fp32_precision = "ieee"
     try:
@@ -567,11 +627,14 @@ def run_gemm(args, metadata) -> None:
     device = torch.device("cuda", args.device)
     sizes = args.sizes
     unit = "TOPS" if key == "int8" else "TFLOP/s"
+    kernel_text = (GEMM_CONFIG[key]["kernel"] if key in GEMM_CONFIG
+                   else "tcgen05 persistent 256x256 tiles (128x256 for MX FP4)")
     print(f"\nMatrix GEMM: {key} inputs, {accumulator_name(key).upper()} accumulate/output; "
-          "2*M*N*K operations; tcgen05 persistent 128x256 tiles")
+          f"2*M*N*K operations; {kernel_text}")
     print("     N  median ms  min ms  median " + unit + "  peak " + unit + "  max abs error")
     info = _native.kernel_info(_native.FAMILY_GEMM, NATIVE[key])
-    audit = compiled_info(key, info, True)
+    probe = metadata.get("tensor_precision_probe")
+    audit = compiled_info(key, info, bool(probe) if key in ("fp32", "tf32", "fp64") else True)
     rows = []
     gen = torch.Generator().manual_seed(args.seed)
     for size in sizes:
@@ -584,7 +647,8 @@ def run_gemm(args, metadata) -> None:
         a, b, scales = gemm_inputs(key, m, n, k, device, gen)
         sa, sb = scales if scales is not None else (None, None)
         c = torch.full((m, n), float("nan") if key != "int8" else 0, device=device,
-                       dtype=torch.int32 if key == "int8" else torch.float32)
+                       dtype=torch.int32 if key == "int8" else
+                       torch.float64 if key == "fp64" else torch.float32)
         if key == "int8":
             c.fill_(-2**31)
         status = torch.zeros(1, dtype=torch.int32, device=device)
@@ -608,19 +672,29 @@ def run_gemm(args, metadata) -> None:
         torch.testing.assert_close(c, reference, rtol=tol, atol=tol)
         max_err = (c.double() - reference.double()).abs().max().item()
         correctness = {"passed": True, "max_abs_error": max_err, "rtol": tol, "atol": tol,
-                       "reference": "FP32 torch.matmul of the decoded operands, IEEE precision"
-                       if key != "int8" else "exact ternary product converted to INT32"}
+                       "reference": "exact ternary product converted to INT32" if key == "int8"
+                       else "FP64 torch.matmul" if key == "fp64"
+                       else "FP32 torch.matmul of the decoded operands, IEEE precision"}
         del reference
         timing = measure(run, args)
         rate = rates(2 * m * n * k, timing, key)
-        row = {**base, "measurement_kind": "dense_tensor_gemm",
+        descriptor = precision_descriptor(args.dtype, args.input_precision)
+        if key in GEMM_CONFIG:
+            config = dict(GEMM_CONFIG[key])
+        else:
+            halves = 1 if key == "fp4" or m <= 128 else 2
+            config = {"block_m": 128 * halves, "block_n": 256, "block_k_bytes": 128,
+                      "stages": 3 if halves == 2 else 4, "persistent": True}
+        row = {**base,
+               "measurement_kind": (f"{descriptor['math_mode']}_gemm"
+                                    if args.dtype in ("fp32", "fp64") else "dense_tensor_gemm"),
                "execution_kind": audit["execution_kind"],
-               "precision_verified": audit["instruction_precision_verified"],
+               "precision_verified": bool(probe) if args.dtype in ("fp32", "fp64")
+               else audit["instruction_precision_verified"],
                "accumulator_dtype": accumulator_name(key), "output_dtype": accumulator_name(key),
-               **precision_descriptor(args.dtype, args.input_precision), **rate,
-               "config": {"block_m": 128, "block_n": 256, "block_k_bytes": 128, "stages": 4,
-                          "persistent": True},
-               "status": "ok", "correctness": correctness, "compiled": audit, **timing}
+               **descriptor, **rate, "config": config,
+               "status": "ok", "correctness": correctness, "precision_probe": probe,
+               "compiled": audit, **timing}
         rows.append(row)
         print(f"{size:6d} {timing['median_ms']:10.4f} {timing['min_ms']:7.4f} "
               f"{rate['median_teraops_per_second']:12.2f} {rate['peak_teraops_per_second']:10.2f} "
@@ -673,10 +747,16 @@ def main(argv=None) -> None:
         key = math_key(args)
         if key not in GEMM_KEYS:
             emit_not_implemented("tensor", metadata, args,
-                                 f"This build's GEMM mode runs on tcgen05 tensor cores "
-                                 f"({', '.join(sorted(GEMM_KEYS))}); {key} GEMM is not "
-                                 "implemented")
+                                 f"This build's GEMM mode covers {', '.join(sorted(GEMM_KEYS))}; "
+                                 f"{key} GEMM is not implemented")
             return
+        if key in ("fp32", "tf32", "fp64"):
+            try:
+                metadata["tensor_precision_probe"] = validate_gemm_precision(
+                    torch.device("cuda", args.device), key)
+            except TensorUnsupportedError as exc:
+                emit_unsupported("tensor", metadata, args, str(exc))
+                return
         run_gemm(args, metadata)
         return
     if not metadata["architecture"].startswith("sm_10"):

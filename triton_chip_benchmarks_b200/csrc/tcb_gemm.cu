@@ -2,7 +2,9 @@
 //
 // A [M][K] and B [N][K] are K-contiguous ("TN"); C [M][N] is fp32 (int32 for
 // INT8).  MX FP4 operands are E2M1 packed two per byte along K with one E8M0
-// scale per 32 elements along K (SA [M][K/32], SB [N][K/32]).
+// scale per 32 elements along K (SA [M][K/32], SB [N][K/32]).  Any M and N, and
+// any K whose rows are whole 16-byte units: edge tiles load zeros past the
+// matrix (TMA out-of-bounds fill) and store only the rows and columns inside.
 //
 // Persistent kernel, one CTA per SM, 256 x 256 output tiles (two M=128
 // accumulators sharing each B tile; 128 x 256 for MX FP4), warp-specialised:
@@ -75,6 +77,7 @@ struct GemmArgs {
   int* status;
   int m, n, kbytes, kgroups;  // kgroups = K/32 scale groups per row
   int tiles_m, tiles_n, kblocks;
+  int vec_store;  // C rows are 16-byte aligned (N % 4 == 0 and C 16-byte aligned)
   uint32_t idesc;
 };
 
@@ -285,17 +288,28 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
 #pragma unroll 1
       for (int h = 0; h < HALVES; ++h) {
         const int row = tm * kTileM + 128 * h + 32 * quarter + lane;
+        const bool row_in = row < args.m;
         uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
         const uint32_t taddr = tbase + ((32u * quarter) << 16) + h * kAccCols;
 #pragma unroll 1
         for (int j = 0; j < kTileN / 32; ++j) {
+          // tcgen05.ld is warp-collective: every lane loads, only in-range rows store.
           uint32_t r[32];
           tmem_ld_32cols(taddr + 32 * j, r);
           tmem_wait_ld();
+          const int col0 = tn * kTileN + 32 * j;
+          if (!row_in || col0 >= args.n) continue;
+          if (args.vec_store && col0 + 32 <= args.n) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2],
-                         r[4 * q + 3]);
+            for (int q = 0; q < 8; ++q)
+              st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2],
+                           r[4 * q + 3]);
+          } else {
+            // Ragged right edge (or unaligned rows): element stores up to N.
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (col0 + q < args.n) dst[32 * j + q] = r[q];
+          }
         }
       }
       tc_fence_before();
@@ -360,8 +374,8 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
 using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
 
 // MX FP4 uses 128 x 256 tiles (its scales need tensor-memory columns); the
-// other kinds use 256 x 256 when M allows it.
-int gemm_halves(int kind, int m) { return kind != gMXF4 && m % 256 == 0 ? 2 : 1; }
+// other kinds use 256 x 256 unless M fits in one 128-row tile.
+int gemm_halves(int kind, int m) { return kind != gMXF4 && m > 128 ? 2 : 1; }
 
 GemmFn gemm_fn(int kind, int halves) {
   if (halves == 2) {
@@ -470,6 +484,7 @@ const char* gemm_instruction(int kind) {
 }  // namespace
 
 int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
+  if (dtype == TCB_T_FP32 || dtype == TCB_T_FP64) return gemm_cuda_core_info(dtype, out);
   const int kind = gemm_kind(dtype);
   if (kind < 0) return TCB_ERR_UNSUPPORTED;
   const int halves = gemm_halves(kind, 256);
@@ -486,46 +501,68 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   return TCB_OK;
 }
 
-// dst[(r/128)][g/8][r%128][g%8] = src[r][g] for E8M0 scales src [rows][groups].
+// Packed E8M0 layout read by the GEMM: rows padded to a multiple of 256 and
+// groups to a multiple of 8 (padding = 127, scale 1.0, so zero-filled operand
+// tails stay zero), then
+//   dst[((r/128) * (groups_p/8) + g/8) * 1024 + (r%128) * 8 + g%8] = src[r][g].
+// Threads walk dst in order, so the stores are coalesced.
 __global__ void mx_scales_pack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
-                                      int rows, int groups) {
-  const long long total = static_cast<long long>(rows) * groups;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i / groups), g = static_cast<int>(i % groups);
-    const long long o = (static_cast<long long>(r / 128) * (groups / 8) + g / 8) * 1024 +
-                        (r % 128) * 8 + (g % 8);
-    dst[o] = src[i];
+                                      int rows, int groups, long long total, int group_blocks) {
+  for (long long o = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < total;
+       o += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long block = o >> 10;
+    const int within = static_cast<int>(o & 1023);
+    const long long r = (block / group_blocks) * 128 + (within >> 3);
+    const int g = static_cast<int>(block % group_blocks) * 8 + (within & 7);
+    dst[o] = r < rows && g < groups ? src[r * groups + g] : static_cast<uint8_t>(127);
   }
+}
+
+long long mx_packed_bytes(int rows, int groups) {
+  return ((static_cast<long long>(rows) + 255) / 256 * 256) * ((groups + 7) / 8 * 8);
 }
 
 }  // namespace tcb
 
 using namespace tcb;
 
+extern "C" long long tcb_mx_scales_packed_bytes(int rows, int groups) {
+  if (rows <= 0 || groups <= 0) return TCB_ERR_INVALID_ARGUMENT;
+  return mx_packed_bytes(rows, groups);
+}
+
 extern "C" int tcb_mx_scales_pack(const void* src, void* dst, int rows, int groups,
                                   tcb_stream_t stream) {
   if (src == nullptr || dst == nullptr || rows <= 0 || groups <= 0) return TCB_ERR_INVALID_ARGUMENT;
-  if (rows % 128 || groups % 8) return TCB_ERR_UNSUPPORTED;
-  if (!aligned(dst, 8)) return TCB_ERR_ALIGNMENT;
+  if (!aligned(dst, 16)) return TCB_ERR_ALIGNMENT;
+  const long long total = mx_packed_bytes(rows, groups);
   clear_stale_error();
-  mx_scales_pack_kernel<<<256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, groups);
+  mx_scales_pack_kernel<<<512, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), rows, groups, total,
+      (groups + 7) / 8);
   return launch_status();
 }
 
 extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA, const void* SB,
                         void* C, int M, int N, int K, int blocks, int* status_dev,
                         tcb_stream_t stream) {
-  const int kind = gemm_kind(dtype);
-  if (kind < 0) return TCB_ERR_UNSUPPORTED;
   if (A == nullptr || B == nullptr || C == nullptr || M <= 0 || N <= 0 || K <= 0 || blocks < 0)
     return TCB_ERR_INVALID_ARGUMENT;
-  if (M % 128 || N % kTileN) return TCB_ERR_UNSUPPORTED;
+  if (dtype == TCB_T_FP32 || dtype == TCB_T_FP64) {
+    DeviceFacts facts;
+    int rc = current_device_facts(&facts);
+    if (rc != TCB_OK) return rc;
+    if (facts.major != 10) return TCB_ERR_UNSUPPORTED;
+    return gemm_cuda_core(dtype, A, B, C, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+  }
+  const int kind = gemm_kind(dtype);
+  if (kind < 0) return TCB_ERR_UNSUPPORTED;
+  // Rows of A and B are TMA rows: their byte length must be a multiple of 16.
+  // M, N and the K tail are free (zero-filled loads, masked stores).
   const long long kbits = static_cast<long long>(K) * gemm_bits(kind);
-  if (kbits % (8 * kBlockBytes)) return TCB_ERR_UNSUPPORTED;
+  if (kbits % 128) return TCB_ERR_UNSUPPORTED;
   if (kind == gMXF4 && (SA == nullptr || SB == nullptr)) return TCB_ERR_INVALID_ARGUMENT;
-  if (!aligned(A, 16) || !aligned(B, 16) || !aligned(C, 16)) return TCB_ERR_ALIGNMENT;
+  if (!aligned(A, 16) || !aligned(B, 16) || !aligned(C, 4)) return TCB_ERR_ALIGNMENT;
   if (kind == gMXF4 && (!aligned(SA, 16) || !aligned(SB, 16))) return TCB_ERR_ALIGNMENT;
   DeviceFacts facts;
   int rc = current_device_facts(&facts);
@@ -546,9 +583,10 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   args.n = N;
   args.kbytes = static_cast<int>(kbytes);
   args.kgroups = K / 32;
-  args.tiles_m = M / tile_m;
-  args.tiles_n = N / kTileN;
-  args.kblocks = static_cast<int>(kbytes / kBlockBytes);
+  args.tiles_m = (M + tile_m - 1) / tile_m;
+  args.tiles_n = (N + kTileN - 1) / kTileN;
+  args.kblocks = static_cast<int>((kbytes + kBlockBytes - 1) / kBlockBytes);
+  args.vec_store = N % 4 == 0 && aligned(C, 16);
   args.idesc = gemm_idesc(kind);
   GemmFn fn = gemm_fn(kind, halves);
   const int smem = gemm_smem(kind, halves);
