@@ -177,3 +177,16 @@ def test_pack_mx_scales_padding():
     assert np.all(packed[packed != 3] == oracle_tensor.E8M0_UNIT_SCALE)
     # row 129, group 16 -> block (1, 2): offset ((1*3 + 2)*1024) + 1*8 + 0
     assert packed[(1 * 3 + 2) * 1024 + 8] == 3 and packed[(1 * 3 + 2) * 1024 + 8 + 1] == 127
+
+
+def test_gemm_inputs_pad_unaligned_k():
+    """Rows that are not whole 16-byte units are zero-padded; aligned K is untouched."""
+    from triton_chip_benchmarks_b200.bench_tensor import gemm_inputs, gemm_padded_k
+    assert gemm_padded_k("int8", 1000) == 1008 and gemm_padded_k("fp4", 1000) == 1024
+    assert gemm_padded_k("bf16", 1000) == 1000 and gemm_padded_k("fp64", 37) == 37
+    gen = torch.Generator().manual_seed(0)
+    a, b, _ = gemm_inputs("int8", 4, 3, 1000, torch.device("cpu"), gen)
+    assert a.shape == (4, 1008) and b.shape == (3, 1008)
+    assert not a[:, 1000:].any() and not b[:, 1000:].any()
+    a, b, _ = gemm_inputs("bf16", 4, 3, 1000, torch.device("cpu"), gen)
+    assert a.shape == (4, 1000)

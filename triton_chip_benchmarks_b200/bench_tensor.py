@@ -565,34 +565,53 @@ GEMM_CONFIG = {
 }
 
 
-def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
-    """A [M,K], B [N,K] (K contiguous), scales for MX FP4, and the FP32 operand values.
+# K elements per 16-byte unit: the tcgen05 GEMM's TMA rows are whole 16-byte
+# units (MX FP4 also whole 32-element scale groups); CUDA-core kinds take any K.
+GEMM_K_UNIT = {"bf16": 8, "fp16": 8, "tf32": 4, "int8": 16, "fp8": 16, "fp4": 32,
+               "fp32": 1, "fp64": 1}
 
-    bf16/fp16/tf32 follow the reference's GEMM inputs (bench_tensor.py:249-261):
-    normal A, normal B scaled by 1/sqrt(K); int8 is ternary; fp8 uses integers in
-    [-3, 3]/4 and fp4 draws all 16 E2M1 codes with unit scales, so those two are
-    exact in FP32.
+
+def gemm_padded_k(key: str, k: int) -> int:
+    unit = GEMM_K_UNIT[key]
+    return -(-k // unit) * unit
+
+
+def gemm_inputs(key: str, m: int, n: int, k: int, device, gen):
+    """A [M,K'], B [N,K'] (K contiguous) and packed scales for MX FP4.
+
+    bf16/fp16/tf32/fp32/fp64 follow the reference's GEMM inputs
+    (bench_tensor.py:249-261): normal A, normal B scaled by 1/sqrt(K); int8 is
+    ternary; fp8 uses integers in [-3, 3]/4 and fp4 draws all 16 E2M1 codes with
+    unit scales, so those two are exact in FP32.  K' = gemm_padded_k(key, k):
+    when K is not a whole number of 16-byte units the rows are zero-padded
+    (data preparation outside timing; the padded columns add nothing to C and
+    the operation count stays 2*M*N*K).
     """
+    kp = gemm_padded_k(key, k)
+
+    def pad(t):
+        return t if kp == k else torch.nn.functional.pad(t, (0, kp - k))
+
     if key == "fp4":
-        a_codes = torch.randint(0, 16, (m, k), generator=gen, dtype=torch.uint8)
-        b_codes = torch.randint(0, 16, (n, k), generator=gen, dtype=torch.uint8)
+        a_codes = pad(torch.randint(0, 16, (m, k), generator=gen, dtype=torch.uint8))
+        b_codes = pad(torch.randint(0, 16, (n, k), generator=gen, dtype=torch.uint8))
         a = pack_e2m1_pairs(a_codes).to(device)
         b = pack_e2m1_pairs(b_codes).to(device)
-        sa = torch.full((m, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
-        sb = torch.full((n, k // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
+        sa = torch.full((m, kp // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
+        sb = torch.full((n, kp // MX_GROUP_SIZE), E8M0_UNIT_SCALE, dtype=torch.uint8, device=device)
         return a, b, (pack_scales(sa), pack_scales(sb))
     if key == "int8":
-        return (torch.randint(-1, 2, (m, k), generator=gen).to(torch.int8).to(device),
-                torch.randint(-1, 2, (n, k), generator=gen).to(torch.int8).to(device), None)
+        return (pad(torch.randint(-1, 2, (m, k), generator=gen).to(torch.int8)).to(device),
+                pad(torch.randint(-1, 2, (n, k), generator=gen).to(torch.int8)).to(device), None)
     if key == "fp8":
-        return ((torch.randint(-3, 4, (m, k), generator=gen).double() / 4)
+        return (pad(torch.randint(-3, 4, (m, k), generator=gen).double() / 4)
                 .to(torch.float8_e4m3fn).to(device),
-                (torch.randint(-3, 4, (n, k), generator=gen).double() / 4)
+                pad(torch.randint(-3, 4, (n, k), generator=gen).double() / 4)
                 .to(torch.float8_e4m3fn).to(device), None)
     dtype = STORAGE[key]
     gen_dtype = torch.float64 if key == "fp64" else torch.float32
-    a = torch.randn((m, k), generator=gen, dtype=gen_dtype).to(dtype).to(device)
-    b = (torch.randn((n, k), generator=gen, dtype=gen_dtype) * (1.0 / math.sqrt(k))) \
+    a = pad(torch.randn((m, k), generator=gen, dtype=gen_dtype)).to(dtype).to(device)
+    b = pad(torch.randn((n, k), generator=gen, dtype=gen_dtype) * (1.0 / math.sqrt(k))) \
         .to(dtype).to(device)
     return a, b, None
 
@@ -653,8 +672,12 @@ def run_gemm(args, metadata) -> None:
             c.fill_(-2**31)
         status = torch.zeros(1, dtype=torch.int32, device=device)
 
+        kp = gemm_padded_k(key, k)
+        if kp != k:
+            base["k_padded"] = kp
+
         def run():
-            _native.gemm(NATIVE[key], a, b, c, m, n, k, scale_a=sa, scale_b=sb, status=status)
+            _native.gemm(NATIVE[key], a, b, c, m, n, kp, scale_a=sa, scale_b=sb, status=status)
 
         try:
             run()
