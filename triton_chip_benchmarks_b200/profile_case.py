@@ -103,21 +103,23 @@ def case_vector(args) -> dict:
 
 
 def case_gemm(args) -> dict:
-    from .bench_tensor import gemm_inputs, gemm_reference
+    from .bench_tensor import GEMM_TOLERANCE, gemm_inputs, gemm_padded_k, gemm_reference
     m = n = k = args.size
+    kp = gemm_padded_k(args.dtype, k)
     gen = torch.Generator().manual_seed(0)
     a, b, scales = gemm_inputs(args.dtype, m, n, k, torch.device("cuda"), gen)
     sa, sb = scales if scales is not None else (None, None)
     c = torch.empty((m, n), device="cuda",
-                    dtype=torch.int32 if args.dtype == "int8" else torch.float32)
+                    dtype=torch.int32 if args.dtype == "int8" else
+                    torch.float64 if args.dtype == "fp64" else torch.float32)
 
     def run():
-        _native.gemm(NATIVE[args.dtype], a, b, c, m, n, k, scale_a=sa, scale_b=sb)
+        _native.gemm(NATIVE[args.dtype], a, b, c, m, n, kp, scale_a=sa, scale_b=sb)
 
     run()
     torch.cuda.synchronize()
     ref = gemm_reference(args.dtype, a, b)
-    tol = 1e-2 if args.dtype in ("bf16", "fp16", "tf32") else 0.0
+    tol = GEMM_TOLERANCE[args.dtype]
     torch.testing.assert_close(c, ref, rtol=tol, atol=tol)
     ms = _time(run, args.launches)
     return {"case": "gemm", "dtype": args.dtype, "size": args.size, "ms_per_launch": ms,
@@ -143,7 +145,7 @@ def main(argv=None):
     p.add_argument("--iterations", type=int, default=4096)
     p.add_argument("--launches", type=int, default=3)
     p = sub.add_parser("gemm")
-    p.add_argument("--dtype", default="bf16", choices=("bf16", "fp16", "tf32", "int8", "fp8", "fp4"))
+    p.add_argument("--dtype", default="bf16", choices=("bf16", "fp16", "tf32", "fp32", "fp64", "int8", "fp8", "fp4"))
     p.add_argument("--size", type=int, default=4096)
     p.add_argument("--launches", type=int, default=3)
     p = sub.add_parser("vector")
