@@ -144,3 +144,97 @@ def test_quick_marks_smoke(tmp_path):
     by = {r["metric"]: r for r in report["results"]}
     assert by["tensor_bf16"].get("smoke_only") is True
     assert not by["memory_bandwidth"].get("smoke_only")
+
+
+# ------------------------------------------------------------- several GPUs
+class FakeProc:
+    def __init__(self, returncode, hang=False):
+        self.returncode = returncode
+        self.hang = hang
+        self.killed = False
+
+    def wait(self, timeout=None):
+        if self.hang and not self.killed:
+            raise subprocess.TimeoutExpired("child", timeout)
+        return self.returncode
+
+    def kill(self):
+        self.killed = True
+
+
+class FakePopen:
+    """Concurrent children: writes each device's document; behaviour per (metric, device)."""
+
+    def __init__(self, behaviour=None, scale=None):
+        self.behaviour = behaviour or {}
+        self.scale = scale or {}
+        self.calls = []
+
+    def __call__(self, command, cwd, stdout, stderr):
+        output = Path(command[command.index("--output") + 1])
+        device = int(command[command.index("--device") + 1])
+        self.calls.append((device, command))
+        key = output.name.split(".gpu")[0]
+        metric = next(m for m in METRICS if m.key == key)
+        action = self.behaviour.get((key, device), "ok")
+        if action == "hang":
+            return FakeProc(None, hang=True)
+        if action == "crash":
+            return FakeProc(2)
+        if action == "unsupported":
+            output.write_text(json.dumps({"status": "unsupported", "reason": "nope"}))
+            return FakeProc(0)
+        document = ok_document(metric)
+        factor = self.scale.get(device, 1.0)
+        for row in document["results"]:
+            for field in ("peak_gbps", "gbps", "peak_teraops_per_second",
+                          "median_teraops_per_second", "peak_tflops", "tflops"):
+                if field in row:
+                    row[field] *= factor
+        output.write_text(json.dumps(document))
+        return FakeProc(0)
+
+
+def test_multi_gpu_table_aggregates_per_gpu_rows(tmp_path, capsys):
+    args = args_for(tmp_path, gpus=2)
+    popen = FakePopen(scale={1: 0.5})
+    report = bench_suite.run_suite(args, popen=popen)
+    assert report["status"] == "complete" and report["n_gpus"] == 2
+    assert sorted({device for device, _ in popen.calls}) == [0, 1]
+    rows = {r["metric"]: r for r in report["results"]}
+    bw = rows["memory_bandwidth"]
+    assert bw["status"] == "ok" and bw["value"] == pytest.approx(6400.0 * 1.5)
+    assert [sub["device_index"] for sub in bw["per_gpu"]] == [0, 1]
+    assert bw["per_gpu"][1]["value"] == pytest.approx(3200.0)
+    assert bw["aggregation"]["n_gpus"] == 2 and bw["aggregation"]["per_gpu_value_min"] == 3200.0
+    assert rows["memory_capacity"]["value"] == pytest.approx(2 * 183.0)
+    assert rows["tensor_bf16"]["median_value"] == pytest.approx(1490.0 * 1.5)
+    assert rows["tensor_bf16"]["execution_kind"] == "tensor"
+    out = capsys.readouterr().out
+    assert "Per GPU:" in out and "GPU 1" in out
+    # the table keeps the single-GPU schema: same 17 keys in the same order
+    assert [r["metric"] for r in report["results"]] == [m.key for m in METRICS]
+
+
+def test_multi_gpu_failure_is_reported_per_gpu(tmp_path):
+    args = args_for(tmp_path, gpus=2, metrics=["tensor_bf16", "vector_fp32", "tensor_fp4"])
+    popen = FakePopen(behaviour={("tensor_bf16", 1): "crash", ("vector_fp32", 0): "hang",
+                                 ("tensor_fp4", 0): "unsupported",
+                                 ("tensor_fp4", 1): "unsupported"})
+    report = bench_suite.run_suite(args, popen=popen)
+    rows = {r["metric"]: r for r in report["results"]}
+    bf16 = rows["tensor_bf16"]
+    assert bf16["status"] == "error" and "GPU 1" in bf16["reason"] and bf16["value"] is None
+    assert bf16["partial_measurement"] == {"gpus": 1, "value": 1500.0}
+    vec = rows["vector_fp32"]
+    assert vec["status"] == "error" and "GPU 0" in vec["reason"]
+    assert "Exceeded" in vec["per_gpu"][0]["reason"]
+    assert rows["tensor_fp4"]["status"] == "unsupported"
+    assert report["status"] == "complete_with_errors"
+
+
+def test_window_overlap():
+    assert bench_suite.window_overlap([(0, 10), (1, 10)]) == pytest.approx(1.0)
+    assert bench_suite.window_overlap([(0, 10), (5, 20)]) == pytest.approx(0.5)
+    assert bench_suite.window_overlap([(0, 1), (2, 3)]) == 0.0
+    assert bench_suite.window_overlap([]) is None

@@ -161,6 +161,76 @@ def summarize(metric: Metric, document: dict) -> dict:
     return result
 
 
+_RUN_KEYS = ("command", "source_json", "log_file", "returncode", "device_index", "window",
+             "patterns", "capacity_bytes", "partial_measurement", "reason", "value",
+             "median_value", "status", "successful_configurations")
+
+
+def aggregate_gpus(metric: Metric, rows: list[dict]) -> dict:
+    """One table row for a metric measured concurrently on several GPUs.
+
+    Each GPU runs its own independent probe (no collective), so the aggregate
+    rate is the sum of the per-GPU peaks (medians) and the capacity the sum of
+    the per-GPU capacities.  The row keeps the single-GPU schema; the detail
+    fields come from the first GPU and every GPU's own row is kept under
+    ``per_gpu``.  A rate is aggregated only when every GPU measured one.
+    """
+    result = empty_metric(metric)
+    measured = [row for row in rows if row.get("status") in ("ok", "unverified")]
+    values = [row.get("value") for row in measured]
+    medians = [row.get("median_value") for row in measured]
+    if rows and len(measured) == len(rows) and all(_is_rate(v) for v in values):
+        result.update({k: v for k, v in rows[0].items() if k not in _RUN_KEYS})
+        result["value"] = sum(values)
+        result["median_value"] = sum(medians) if all(_is_rate(v) for v in medians) else None
+        unverified = [row for row in rows if row["status"] == "unverified"]
+        result["status"] = "unverified" if unverified else "ok"
+        if unverified:
+            result["reason"] = unverified[0].get("reason")
+        if metric.key == "memory_capacity":
+            result["capacity_bytes"] = sum(row.get("capacity_bytes", 0) for row in rows)
+    else:
+        statuses = {row.get("status") for row in rows}
+        if len(statuses) == 1 and statuses <= {"unsupported", "not_implemented",
+                                               "not_measured", "unavailable"}:
+            result.update(status=statuses.pop(), reason=rows[0].get("reason"))
+        else:
+            failed = [row for row in rows if row not in measured]
+            result.update(status="error", reason="; ".join(
+                f"GPU {row.get('device_index', i)}: {row.get('status')}"
+                + (f" ({row['reason']})" if row.get("reason") else "")
+                for i, row in enumerate(failed)) or "no GPU produced a rate")
+            if measured and all(_is_rate(v) for v in values):
+                result["partial_measurement"] = {"gpus": len(measured), "value": sum(values)}
+    per_gpu_values = [v for v in values if _is_rate(v)]
+    result["aggregation"] = {
+        "n_gpus": len(rows),
+        "method": ("sum over GPUs of each GPU's value from concurrent, independent runs "
+                   "(no collective)"),
+        "per_gpu_value_min": min(per_gpu_values, default=None),
+        "per_gpu_value_max": max(per_gpu_values, default=None),
+    }
+    result["per_gpu"] = rows
+    return result
+
+
+def format_per_gpu(results: list[dict]) -> str:
+    """Metric x GPU table of the per-GPU values (empty when no row has per-GPU data)."""
+    rows = [item for item in results if item.get("per_gpu")]
+    if not rows:
+        return ""
+    devices = [sub.get("device_index", i) for i, sub in enumerate(rows[0]["per_gpu"])]
+    header = f"{'Metric':<20} " + " ".join(f"{'GPU ' + str(d):>11}" for d in devices)
+    lines = [header, "-" * len(header)]
+    for item in rows:
+        cells = []
+        for sub in item["per_gpu"]:
+            value = sub.get("value")
+            cells.append(f"{value:>11.3f}" if _is_rate(value) else f"{sub.get('status', '-'):>11}")
+        lines.append(f"{item['metric']:<20} " + " ".join(cells))
+    return "\n".join(lines)
+
+
 def format_table(results: list[dict]) -> str:
     """One line per requested metric, including missing results, then notes."""
     lines = [f"{'Metric':<20} {'Peak / capacity':>17} {'Median':>12} {'Unit':<8} Status",
