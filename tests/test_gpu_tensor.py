@@ -259,6 +259,28 @@ def test_gemm_persistent_tiles(cuda, native):
     assert np.array_equal(c.cpu().double().numpy(), ref)
 
 
+def test_gemm_mxf4_pairs_walk_several_tiles(cuda, native):
+    """MX FP4 on CTA pairs: 2 pairs walk 16 tiles of 256 x 256, per-group scales."""
+    m, n, k = 1024, 1024, 512
+    a, b = _operands(MXF4, 1, 1, m, n, k, seed=11)
+    a, b = a[0], b[0, 0]
+    gen = torch.Generator().manual_seed(12)
+    sa = torch.randint(124, 131, (m, k // 32), generator=gen, dtype=torch.uint8)
+    sb = torch.randint(124, 131, (n, k // 32), generator=gen, dtype=torch.uint8)
+    psa = torch.empty(native.mx_scales_packed_bytes(m, k // 32), dtype=torch.uint8, device=cuda)
+    psb = torch.empty(native.mx_scales_packed_bytes(n, k // 32), dtype=torch.uint8, device=cuda)
+    native.mx_scales_pack(sa.to(cuda), psa, m, k // 32)
+    native.mx_scales_pack(sb.to(cuda), psb, n, k // 32)
+    c = torch.full((m, n), -7.0, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    native.gemm(MXF4, a.to(cuda), b.to(cuda), c, m, n, k, scale_a=psa, scale_b=psb, blocks=4,
+                status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = oracle_tensor.resident_reference(a.numpy(), b.numpy(), 1, "fp4", sa.numpy(), sb.numpy())
+    assert np.array_equal(c.cpu().double().numpy(), ref)
+
+
 def test_gemm_rejects_unsupported_shapes(cuda, native):
     # K = 60 bf16 elements: a 120-byte row is not a whole number of 16-byte units.
     a = torch.zeros((128, 60), dtype=torch.bfloat16, device=cuda)

@@ -33,19 +33,23 @@
 #include <cudaTypedefs.h>
 
 #include "tcb_device.cuh"
+#include "tcb_gemm_common.cuh"
 #include "tcb_host.h"
 #include "tcb_registry.h"
 
 namespace tcb {
 namespace {
 
-enum GKind : int { gF16 = 0, gBF16 = 1, gTF32 = 2, gI8 = 3, gE4M3 = 4, gMXF4 = 5 };
+using namespace gemm_detail;
 
-constexpr int kTileN = 256;
-constexpr int kBlockBytes = 128;     // K bytes per pipeline stage (one SWIZZLE_128B panel)
-constexpr int kStepsPerBlock = 4;    // 32-byte MMA K steps per block
-constexpr int kAccCols = kTileN;     // fp32 accumulator columns per M=128 half
-constexpr int kSmemBudget = 227 * 1024 - 1024;
+}  // namespace
+
+int gemm_pair_launch(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_c,
+                     const GemmArgs& args, int pairs, const DeviceFacts& facts,
+                     cudaStream_t stream);
+int gemm_pair_info(tcb_kernel_info_t* out);
+
+namespace {
 
 // Tile geometry: HALVES M=128 accumulators share each B tile.  A 256 x 256
 // tile (two halves) feeds the tensor cores with 64 KB per 1024 MMA cycles
@@ -60,77 +64,10 @@ struct Tile {
   // MX FP4: the packed E8M0 scales of the block (A: kM x 8 B, B: 256 x 8 B).
   static constexpr int kStageS = SCALED ? (kM + kTileN) * 8 : 0;
   static constexpr int kStageBytes = kStageA + kStageB + kStageS;
-  static constexpr int kStages = kSmemBudget / kStageBytes > 6 ? 6 : kSmemBudget / kStageBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024;
+  static constexpr int kRing = kSmemBudget - kEpiSmem;  // the rest stages C for TMA stores
+  static constexpr int kStages = kRing / kStageBytes > 6 ? 6 : kRing / kStageBytes;
+  static constexpr int kSmem = kStages * kStageBytes + kEpiSmem + 1024;
 };
-constexpr int kSfStepCols = 4 + kTileN / 32;    // A: 4 columns, B: 8 columns per K step
-constexpr int kMaxStages = 6;
-constexpr int kSfStageCols = kStepsPerBlock * kSfStepCols;
-constexpr int kTmemCols = 512;
-constexpr int kEpilogueWarps = 4;
-constexpr int kScaleWarps = 4;
-
-struct GemmArgs {
-  const uint8_t* sa;  // [M][K/32] E8M0 (MX FP4)
-  const uint8_t* sb;  // [N][K/32]
-  uint32_t* c;        // [M][N] 32-bit
-  int* status;
-  int m, n, kbytes, kgroups;  // kgroups = K/32 scale groups per row
-  int tiles_m, tiles_n, kblocks;
-  int vec_store;  // C rows are 16-byte aligned (N % 4 == 0 and C 16-byte aligned)
-  uint32_t idesc;
-};
-
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
-                                              volatile int* abort_flag, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long start = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - start > kWaitTimeoutNs) {
-      *abort_flag = 1;
-      report_status(status, TCB_ERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
-}
-
-// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
-__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t size,
-                                             uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(smem_dst)),
-      "l"(src), "r"(size), "r"(smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-// Tile t -> (tm, tn) in groups of kGroupM row-blocks: the tiles a wave of
-// persistent CTAs works on at once share few A row-blocks and B column-blocks,
-// so their operands stay in L2.
-constexpr int kGroupM = 8;
-
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int* tm, int* tn) {
-  const int per_group = kGroupM * tiles_n;
-  const int group = t / per_group;
-  const int first = group * kGroupM;
-  const int rows = min(tiles_m - first, kGroupM);
-  const int r = t - group * per_group;
-  *tm = first + r % rows;
-  *tn = r / rows;
-}
-
-__device__ __forceinline__ void st_stream_u4(void* p, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
-}
 
 template <int KIND>
 __device__ __forceinline__ void gemm_mma(uint32_t d, uint64_t adesc, uint64_t bdesc,
@@ -163,7 +100,8 @@ __device__ __forceinline__ void gemm_mma(uint32_t d, uint64_t adesc, uint64_t bd
 template <int KIND, int HALVES>
 __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a,
-                const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+                const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_c, const GemmArgs args) {
   constexpr bool kScaled = KIND == gMXF4;
   using T = Tile<HALVES, kScaled>;
   constexpr int kStages = T::kStages;
@@ -188,6 +126,7 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_b);
+    if (args.tma_store) prefetch_tensormap(&map_c);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&loaded[s], 1);
       mbar_init(&full[s], kScaleWarps);
@@ -278,44 +217,41 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
   } else if (warp < 2 + kEpilogueWarps) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
-    int ti = 0;
+    uint8_t* epi_stage = smem + kStages * kStageBytes + (warp - 2) * kEpiWarpBytes;
+    int ti = 0, issued = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ti) {
       if (!wait_or_abort(&acc_full, static_cast<uint32_t>(ti) & 1u, &abort_flag, args.status))
         break;
       tc_fence_after();
       int tm, tn;
       tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
+      // 64-column round trips per M=128 half.  The accumulator is released
+      // once its last columns are in registers, so C traffic overlaps the
+      // next tile's MMAs.
+      uint32_t r[kEpiChunks][32];
 #pragma unroll 1
       for (int h = 0; h < HALVES; ++h) {
-        const int row = tm * kTileM + 128 * h + 32 * quarter + lane;
+        const int row0 = tm * kTileM + 128 * h + 32 * quarter;
+        const uint32_t taddr = tbase + ((32u * quarter) << 16) + h * kAccCols;
+        const int row = row0 + lane;
         const bool row_in = row < args.m;
         uint32_t* dst = args.c + static_cast<size_t>(row) * args.n + tn * kTileN;
-        const uint32_t taddr = tbase + ((32u * quarter) << 16) + h * kAccCols;
 #pragma unroll 1
-        for (int j = 0; j < kTileN / 32; ++j) {
-          // tcgen05.ld is warp-collective: every lane loads, only in-range rows store.
-          uint32_t r[32];
-          tmem_ld_32cols(taddr + 32 * j, r);
-          tmem_wait_ld();
-          const int col0 = tn * kTileN + 32 * j;
-          if (!row_in || col0 >= args.n) continue;
-          if (args.vec_store && col0 + 32 <= args.n) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              st_stream_u4(dst + 32 * j + 4 * q, r[4 * q], r[4 * q + 1], r[4 * q + 2],
-                           r[4 * q + 3]);
-          } else {
-            // Ragged right edge (or unaligned rows): element stores up to N.
-#pragma unroll
-            for (int q = 0; q < 32; ++q)
-              if (col0 + q < args.n) dst[32 * j + q] = r[q];
+        for (int c0 = 0; c0 < kTileN; c0 += 32 * kEpiChunks) {
+          acc_load<kEpiChunks>(taddr + c0, r);
+          if (h + 1 == HALVES && c0 + 32 * kEpiChunks == kTileN) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty);
           }
+          if (args.tma_store)
+            acc_tma_store<kEpiChunks>(&map_c, epi_stage, lane, r, tn * kTileN + c0, row0, issued);
+          else if (row_in)
+            acc_store<kEpiChunks>(dst + c0, r, tn * kTileN + c0, args.n, args.vec_store);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty);
     }
+    if (lane == 0) bulk_wait_group_all();  // C stores complete before the CTA retires
   } else if (kScaled) {
     // ------------------------------------------------------ scale writers
     // The producer brings each block's packed scales into the stage with the
@@ -371,7 +307,7 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
   }
 }
 
-using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
+using GemmFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 
 // MX FP4 uses 128 x 256 tiles (its scales need tensor-memory columns); the
 // other kinds use 256 x 256 unless M fits in one 128-row tile.
@@ -428,8 +364,8 @@ int gemm_bits(int kind) {
   return 0;
 }
 
-uint32_t gemm_idesc(int kind) {
-  uint32_t d = static_cast<uint32_t>(kTileN >> 3) << 17 | static_cast<uint32_t>(128 >> 4) << 24;
+uint32_t gemm_idesc(int kind, int mma_m = 128) {
+  uint32_t d = static_cast<uint32_t>(kTileN >> 3) << 17 | static_cast<uint32_t>(mma_m >> 4) << 24;
   if (kind == gMXF4) return d | 1u << 7 | 1u << 10 | 1u << 23;
   uint32_t c_fmt = 1, ab = 0;
   if (kind == gBF16) ab = 1;
@@ -466,6 +402,21 @@ int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_b
 }
 
 
+// C [M][N] of 32-bit elements, 32 x 32 boxes in the SWIZZLE_128B layout the
+// epilogue stages; needs N % 4 == 0 (16-byte row pitch) and a 16-byte base.
+int gemm_map_c(CUtensorMap* map, void* base, int rows, int cols) {
+  auto fn = gemm_encode_fn();
+  if (fn == nullptr) return TCB_ERR_DEVICE;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TCB_OK : TCB_ERR_INVALID_ARGUMENT;
+}
+
 // The arithmetic instruction each kind's kernel writes, in the same wording as
 // the resident probe's table (operand and accumulator types spelled out).
 const char* gemm_instruction(int kind) {
@@ -487,6 +438,14 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   if (dtype == TCB_T_FP32 || dtype == TCB_T_FP64) return gemm_cuda_core_info(dtype, out);
   const int kind = gemm_kind(dtype);
   if (kind < 0) return TCB_ERR_UNSUPPORTED;
+  if (kind == gMXF4) {
+    const int rc = gemm_pair_info(out);
+    if (rc != TCB_OK) return rc;
+    copy_str(out->instruction, sizeof(out->instruction),
+             "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 (e2m1 x e2m1, ue8m0 -> f32)");
+    copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
+    return TCB_OK;
+  }
   const int halves = gemm_halves(kind, 256);
   cudaFuncAttributes attr;
   if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind, halves))) !=
@@ -568,9 +527,37 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   int rc = current_device_facts(&facts);
   if (rc != TCB_OK) return rc;
   if (facts.major != 10) return TCB_ERR_UNSUPPORTED;
+  const long long kbytes = kbits / 8;
+  if (kind == gMXF4 && M > 128) {
+    // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of A and of B.
+    CUtensorMap map_a, map_b;
+    if ((rc = gemm_map(&map_a, A, M, kbytes, 128)) != TCB_OK) return rc;
+    if ((rc = gemm_map(&map_b, B, N, kbytes, 128)) != TCB_OK) return rc;
+    GemmArgs args;
+    args.sa = static_cast<const uint8_t*>(SA);
+    args.sb = static_cast<const uint8_t*>(SB);
+    args.c = static_cast<uint32_t*>(C);
+    args.status = status_dev;
+    args.m = M;
+    args.n = N;
+    args.kbytes = static_cast<int>(kbytes);
+    args.kgroups = K / 32;
+    args.tiles_m = (M + 255) / 256;
+    args.tiles_n = (N + kTileN - 1) / kTileN;
+    args.kblocks = static_cast<int>((kbytes + kBlockBytes - 1) / kBlockBytes);
+    args.vec_store = N % 4 == 0 && aligned(C, 16);
+    CUtensorMap map_c{};
+    args.tma_store = args.vec_store && gemm_map_c(&map_c, C, M, N) == TCB_OK;
+    args.idesc = gemm_idesc(kind, 256);
+    const int tiles = args.tiles_m * args.tiles_n;
+    int pairs = blocks > 0 ? blocks / 2 : facts.sm_count / 2;
+    if (pairs < 1) pairs = 1;
+    if (pairs > tiles) pairs = tiles;
+    return gemm_pair_launch(map_a, map_b, map_c, args, pairs, facts,
+                            reinterpret_cast<cudaStream_t>(stream));
+  }
   const int halves = gemm_halves(kind, M);
   const int tile_m = 128 * halves;
-  const long long kbytes = kbits / 8;
   CUtensorMap map_a, map_b;
   if ((rc = gemm_map(&map_a, A, M, kbytes, tile_m)) != TCB_OK) return rc;
   if ((rc = gemm_map(&map_b, B, N, kbytes, kTileN)) != TCB_OK) return rc;
@@ -587,6 +574,8 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   args.tiles_n = (N + kTileN - 1) / kTileN;
   args.kblocks = static_cast<int>((kbytes + kBlockBytes - 1) / kBlockBytes);
   args.vec_store = N % 4 == 0 && aligned(C, 16);
+  CUtensorMap map_c{};
+  args.tma_store = args.vec_store && gemm_map_c(&map_c, C, M, N) == TCB_OK;
   args.idesc = gemm_idesc(kind);
   GemmFn fn = gemm_fn(kind, halves);
   const int smem = gemm_smem(kind, halves);
@@ -605,6 +594,6 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   if (blocks > tiles) blocks = tiles;
   clear_stale_error();
   fn<<<blocks, (6 + kScaleWarps) * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      map_a, map_b, args);
+      map_a, map_b, map_c, args);
   return launch_status();
 }
