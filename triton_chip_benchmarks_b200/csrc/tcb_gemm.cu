@@ -204,8 +204,9 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
               // Half h of A starts 128 rows (16 KB) further into the stage.
               const uint64_t ad =
                   desc_const | (a_lo + static_cast<uint32_t>(h * (128 * kBlockBytes >> 4) + k * 2));
-              gemm_mma<KIND>(tbase + h * kAccCols, ad, bd, args.idesc, (kb | k) != 0,
-                             sf + k * kSfStepCols, sf + k * kSfStepCols + 4);
+              gemm_mma<KIND>(tbase + h * kAccCols, ad, bd,
+                             kScaled ? sf_idesc(args.idesc, k) : args.idesc, (kb | k) != 0,
+                             sf_cols_a(sf, k), sf_cols_b(sf, k));
             }
           }
           tc_commit(&empty[s]);
@@ -272,25 +273,7 @@ __global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
 #pragma unroll
         for (int j = 0; j < kTileN / 32; ++j)
           fb[j] = *reinterpret_cast<const uint2*>(ss + 1024 + 256 * j);
-        const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
-#pragma unroll
-        for (int k = 0; k < kStepsPerBlock; ++k) {
-          uint32_t va[4], vb[kTileN / 32];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t w = k < 2 ? fa[j].x : fa[j].y;
-            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            va[j] = v | (v << 16);
-          }
-#pragma unroll
-          for (int j = 0; j < kTileN / 32; ++j) {
-            const uint32_t w = k < 2 ? fb[j].x : fb[j].y;
-            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            vb[j] = v | (v << 16);
-          }
-          tmem_st_4cols(lane_base + col0 + k * kSfStepCols, va);
-          tmem_st_8cols(lane_base + col0 + k * kSfStepCols + 4, vb);
-        }
+        write_scale_slot(lane_base + static_cast<uint32_t>(s * kSfStageCols), fa, fb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();

@@ -18,9 +18,40 @@ constexpr int kStepsPerBlock = 4;    // 32-byte MMA K steps per block
 constexpr int kAccCols = kTileN;     // fp32 accumulator columns per M=128 half
 constexpr int kSmemBudget = 227 * 1024 - 1024;
 
-constexpr int kSfStepCols = 4 + kTileN / 32;    // A: 4 columns, B: 8 columns per K step
+// MX scales in tensor memory: one 32-bit column word holds the scale pairs of
+// two consecutive K steps (bytes 0-1 and 2-3), selected per MMA by the scale
+// factor ID of the instruction descriptor (0 or 2).  A takes 4 columns and B 8
+// columns per pair of K steps.
+constexpr int kSfPairCols = 4 + kTileN / 32;
 constexpr int kMaxStages = 6;
-constexpr int kSfStageCols = kStepsPerBlock * kSfStepCols;
+constexpr int kSfStageCols = (kStepsPerBlock / 2) * kSfPairCols;
+
+// Scale-factor columns and descriptor of K step k of a block whose scale slot
+// starts at column `sf`.
+__device__ __forceinline__ uint32_t sf_cols_a(uint32_t sf, int k) { return sf + (k >> 1) * kSfPairCols; }
+__device__ __forceinline__ uint32_t sf_cols_b(uint32_t sf, int k) {
+  return sf + (k >> 1) * kSfPairCols + 4;
+}
+__device__ __forceinline__ uint32_t sf_idesc(uint32_t idesc, int k) {
+  const uint32_t id = 2u * static_cast<uint32_t>(k & 1);
+  return idesc | (id << 29) | (id << 4);  // A scale factor ID [29,31), B [4,6)
+}
+
+// Stage scale records (8 bytes = groups 0-7 of one row's K block) into tensor
+// memory: word x covers K steps 0-1, word y K steps 2-3, as staged.
+__device__ __forceinline__ void write_scale_slot(uint32_t lane_col0, const uint2 (&fa)[4],
+                                                 const uint2 (&fb)[kTileN / 32]) {
+#pragma unroll
+  for (int kp = 0; kp < 2; ++kp) {
+    uint32_t va[4], vb[kTileN / 32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) va[j] = kp == 0 ? fa[j].x : fa[j].y;
+#pragma unroll
+    for (int j = 0; j < kTileN / 32; ++j) vb[j] = kp == 0 ? fb[j].x : fb[j].y;
+    tmem_st_4cols(lane_col0 + kp * kSfPairCols, va);
+    tmem_st_8cols(lane_col0 + kp * kSfPairCols + 4, vb);
+  }
+}
 constexpr int kTmemCols = 512;
 constexpr int kEpilogueWarps = 4;
 constexpr int kScaleWarps = 4;

@@ -177,8 +177,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int k = 0; k < kStepsPerBlock; ++k) {
             pair_mma_mxf4(tbase, desc_const | (a_lo + static_cast<uint32_t>(k * 2)),
-                          desc_const | (b_lo + static_cast<uint32_t>(k * 2)), args.idesc,
-                          (kb | k) != 0, sf + k * kSfStepCols, sf + k * kSfStepCols + 4);
+                          desc_const | (b_lo + static_cast<uint32_t>(k * 2)),
+                          sf_idesc(args.idesc, k), (kb | k) != 0, sf_cols_a(sf, k),
+                          sf_cols_b(sf, k));
           }
           tc_commit_pair(&empty[s], 0x3);
         }
@@ -229,8 +230,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   } else {
     // ------------------------------------------------------ scale writers
     // Lane l takes rows 32j+l (8 bytes each) of the staged scales and writes
-    // them into this CTA's scale slot for the stage, one 16-bit pair per K
-    // step, repeated in both halves of the 32-bit column.
+    // them into this CTA's scale slot for the stage (two K steps per word).
     const int quarter = warp & 3;
     const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
     int it = 0;
@@ -246,25 +246,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int j = 0; j < kTileN / 32; ++j)
           fb[j] = *reinterpret_cast<const uint2*>(ss + 1024 + 256 * j);
-        const uint32_t col0 = static_cast<uint32_t>(s * kSfStageCols);
-#pragma unroll
-        for (int k = 0; k < kStepsPerBlock; ++k) {
-          uint32_t va[4], vb[kTileN / 32];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t w = k < 2 ? fa[j].x : fa[j].y;
-            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            va[j] = v | (v << 16);
-          }
-#pragma unroll
-          for (int j = 0; j < kTileN / 32; ++j) {
-            const uint32_t w = k < 2 ? fb[j].x : fb[j].y;
-            const uint32_t v = (w >> (16 * (k & 1))) & 0xFFFFu;
-            vb[j] = v | (v << 16);
-          }
-          tmem_st_4cols(lane_base + col0 + k * kSfStepCols, va);
-          tmem_st_8cols(lane_base + col0 + k * kSfStepCols + 4, vb);
-        }
+        write_scale_slot(lane_base + static_cast<uint32_t>(s * kSfStageCols), fa, fb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
