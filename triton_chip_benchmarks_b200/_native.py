@@ -38,7 +38,7 @@ FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR, FAMILY_GEMM = 0, 1, 2, 3
 # Every symbol include/tcb.h declares.
 EXPORTED_SYMBOLS = (
     "tcb_strerror", "tcb_version", "tcb_device_query", "tcb_copy", "tcb_read",
-    "tcb_vector_chains", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_packed_bytes",
+    "tcb_vector_chains", "tcb_vector_chains_imm", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_packed_bytes",
     "tcb_mx_scales_pack", "tcb_kernel_info",
 )
 
@@ -128,6 +128,7 @@ def load() -> ctypes.CDLL:
         lib.tcb_copy.argtypes = [vp, vp, sz, i, i, i, vp]
         lib.tcb_read.argtypes = [vp, i, ll, vp, i, i, vp]
         lib.tcb_vector_chains.argtypes = [i, vp, vp, vp, ll, i, i, i, i, i, vp]
+        lib.tcb_vector_chains_imm.argtypes = [i, vp, vp, vp, ll, i, i, i, i, i, vp]
         lib.tcb_tensor_peak.argtypes = [i, i, vp, vp, vp, vp, vp, i, i, i, i, i, i, i, vp, vp]
         lib.tcb_gemm.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_mx_scales_pack.argtypes = [vp, vp, i, i, vp]
@@ -217,9 +218,18 @@ def read(src, dtype: int, elements: int, sink, block_elems: int, threads: int = 
 def vector_chains(dtype: int, inputs, outputs, coefficients, elements: int, iterations: int,
                   blocks: int, threads: int, elems_per_thread: int, unroll: int,
                   stream=None) -> None:
-    check(load().tcb_vector_chains(dtype, _ptr(inputs), _ptr(outputs), _ptr(coefficients),
-                                   elements, iterations, blocks, threads, elems_per_thread,
-                                   unroll, _stream(stream)), "tcb_vector_chains")
+    """Coefficients on the device -> tcb_vector_chains; in host memory (a CPU
+    tensor or numpy array) -> tcb_vector_chains_imm (passed to the kernel by value)."""
+    on_device = getattr(coefficients, "is_cuda", False)
+    if not on_device and hasattr(coefficients, "is_contiguous") and \
+            not coefficients.is_contiguous():
+        raise ValueError("host coefficients must be contiguous")
+    fn = load().tcb_vector_chains if on_device else load().tcb_vector_chains_imm
+    name = "tcb_vector_chains" if on_device else "tcb_vector_chains_imm"
+    host_ptr = _ptr(coefficients) if on_device or not hasattr(coefficients, "ctypes") \
+        else coefficients.ctypes.data
+    check(fn(dtype, _ptr(inputs), _ptr(outputs), host_ptr, elements, iterations, blocks, threads,
+             elems_per_thread, unroll, _stream(stream)), name)
 
 
 def tensor_peak(dtype: int, variant: int, a, b, c, *, blocks: int, blocks_per_sm: int,

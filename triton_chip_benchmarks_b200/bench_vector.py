@@ -200,6 +200,7 @@ def run_benchmark(args, metadata):
                 raise SystemExit(f"Vector input/output need {need / 2**30:.2f} GiB; "
                                  "reduce --blocks-per-sm or --block-sizes")
             inputs, coeff = make_inputs(args, elements, device)
+            coeff_host = coeff.cpu()
             output = torch.empty_like(inputs)
             for warps in args.num_warps:
                 threads = warps * 32
@@ -222,8 +223,10 @@ def run_benchmark(args, metadata):
 
                     def run(iterations=args.iterations, unroll_value=unroll,
                             per_thread=per_thread, threads=threads):
-                        _native.vector_chains(ndtype, inputs, output, coeff, elements, iterations,
-                                              blocks, threads, per_thread, unroll_value)
+                        # Host coefficients: passed to the kernel by value.
+                        _native.vector_chains(ndtype, inputs, output, coeff_host, elements,
+                                              iterations, blocks, threads, per_thread,
+                                              unroll_value)
 
                     sentinel(output, -128 if store == torch.int8 else -(2**31) if is_int
                              else float("nan"))
@@ -278,7 +281,7 @@ def run_benchmark(args, metadata):
                         if is_int else args.dtype,
                         "includes_unpacking": False,
                         "operation": operation, "input_pattern": args.inputs,
-                        "loop_structure": "strip_mined", "coefficient_load": "scalar",
+                        "loop_structure": "strip_mined", "coefficient_load": "kernel_parameter",
                         "hardware_fusion_verified": not is_int,
                         "explicit_fma_supported": not is_int,
                         "dp4a_used": is_int and args.int8_op == "dp4a",

@@ -149,11 +149,24 @@ struct Mem<OpI8MulAdd> {
   }
 };
 
-// in/out: [8][elements] storage; words are kPack elements wide.
-template <typename Op, int ELEMS, int UNROLL>
+// Coefficients {a, b_0..b_7} passed by value: they live in the kernel
+// parameter (constant) bank, so the compiler can feed them to the FMA as
+// constant-bank operands instead of registers.  For FP64 this matters: a
+// DFMA with three register-resident 64-bit operands ran at 92 % of the FP64
+// pipe, one with constant-bank coefficients at 99.7 %.
+template <typename Op>
+struct CoeffImm {
+  typename Op::Word v[1 + kChains];
+};
+
+// in/out: [8][elements] storage; words are kPack elements wide.  IMM selects
+// the coefficient source: the by-value parameter `imm`, or device memory at
+// `coeff` (loaded once into registers).
+template <typename Op, int ELEMS, int UNROLL, bool IMM>
 __global__ void __launch_bounds__(1024)
     chains_kernel(const void* __restrict__ in, void* __restrict__ out,
-                  const void* __restrict__ coeff, long long words_per_chain, int iterations) {
+                  const void* __restrict__ coeff, const __grid_constant__ CoeffImm<Op> imm,
+                  long long words_per_chain, int iterations) {
   using Word = typename Op::Word;
   constexpr int kSlots = ELEMS / Op::kPack;
   const long long block_words = static_cast<long long>(blockDim.x) * kSlots;
@@ -166,29 +179,34 @@ __global__ void __launch_bounds__(1024)
     for (int i = 0; i < kSlots; ++i)
       x[c][i] = Mem<Op>::load(in, c * words_per_chain + first + i * blockDim.x);
 
-  const Word a = Mem<Op>::coeff(coeff, 0);
-  Word b[kChains];
+  Word a_reg{}, b_reg[kChains]{};
+  if constexpr (!IMM) {
+    a_reg = Mem<Op>::coeff(coeff, 0);
 #pragma unroll
-  for (int c = 0; c < kChains; ++c) b[c] = Mem<Op>::coeff(coeff, 1 + c);
+    for (int c = 0; c < kChains; ++c) b_reg[c] = Mem<Op>::coeff(coeff, 1 + c);
+  }
+  // One update of every accumulator.
+  auto sweep = [&]() {
+#pragma unroll
+    for (int c = 0; c < kChains; ++c)
+#pragma unroll
+      for (int i = 0; i < kSlots; ++i) {
+        if constexpr (IMM)
+          Op::step(x[c][i], imm.v[0], imm.v[1 + c]);
+        else
+          Op::step(x[c][i], a_reg, b_reg[c]);
+      }
+  };
 
   const int full = iterations / UNROLL;
   const int rest = iterations - full * UNROLL;
 #pragma unroll 1
   for (int it = 0; it < full; ++it) {
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-      for (int c = 0; c < kChains; ++c)
-#pragma unroll
-        for (int i = 0; i < kSlots; ++i) Op::step(x[c][i], a, b[c]);
+    for (int u = 0; u < UNROLL; ++u) sweep();
   }
 #pragma unroll 1
-  for (int it = 0; it < rest; ++it) {
-#pragma unroll
-    for (int c = 0; c < kChains; ++c)
-#pragma unroll
-      for (int i = 0; i < kSlots; ++i) Op::step(x[c][i], a, b[c]);
-  }
+  for (int it = 0; it < rest; ++it) sweep();
 
 #pragma unroll
   for (int c = 0; c < kChains; ++c)
@@ -197,7 +215,8 @@ __global__ void __launch_bounds__(1024)
       Mem<Op>::store(out, c * words_per_chain + first + i * blockDim.x, x[c][i]);
 }
 
-using ChainFn = void (*)(const void*, void*, const void*, long long, int);
+template <typename Op>
+using ChainFnT = void (*)(const void*, void*, const void*, CoeffImm<Op>, long long, int);
 
 constexpr int kElemChoices[] = {1, 2, 4, 8, 16};
 constexpr int kUnrollChoices[] = {1, 2, 4, 8, 16};
@@ -215,89 +234,145 @@ int unroll_index(int u) {
 
 // Table [elems][unroll] of kernel instantiations for one op.  16-bit ops
 // have no ELEMS=1 variant (a packed pair holds two elements).
-template <typename Op, int E>
+template <typename Op, int E, bool IMM>
 struct Row {
-  static constexpr ChainFn fns[5] = {chains_kernel<Op, E, 1>, chains_kernel<Op, E, 2>,
-                                     chains_kernel<Op, E, 4>, chains_kernel<Op, E, 8>,
-                                     chains_kernel<Op, E, 16>};
+  static constexpr ChainFnT<Op> fns[5] = {
+      chains_kernel<Op, E, 1, IMM>, chains_kernel<Op, E, 2, IMM>, chains_kernel<Op, E, 4, IMM>,
+      chains_kernel<Op, E, 8, IMM>, chains_kernel<Op, E, 16, IMM>};
 };
 
-template <typename Op>
-ChainFn pick(int e, int u) {
+template <typename Op, bool IMM>
+ChainFnT<Op> pick(int e, int u) {
   const int ei = elem_index(e), ui = unroll_index(u);
   if (ei < 0 || ui < 0) return nullptr;
   if (Op::kPack == 2 && e == 1) return nullptr;
   switch (e) {
     case 1:
-      if constexpr (Op::kPack == 1) return Row<Op, 1>::fns[ui];
+      if constexpr (Op::kPack == 1) return Row<Op, 1, IMM>::fns[ui];
       return nullptr;
     case 2:
-      return Row<Op, 2>::fns[ui];
+      return Row<Op, 2, IMM>::fns[ui];
     case 4:
-      return Row<Op, 4>::fns[ui];
+      return Row<Op, 4, IMM>::fns[ui];
     case 8:
-      return Row<Op, 8>::fns[ui];
+      return Row<Op, 8, IMM>::fns[ui];
     case 16:
-      return Row<Op, 16>::fns[ui];
+      return Row<Op, 16, IMM>::fns[ui];
   }
   return nullptr;
 }
 
-struct Choice {
-  ChainFn fn = nullptr;
+// Coefficients as the kernels use them, from host memory in the storage type
+// (packed 16-bit pairs repeat the scalar; int8 is sign-extended).
+template <typename Op>
+CoeffImm<Op> host_coeffs(const void* host) {
+  CoeffImm<Op> c{};
+  for (int i = 0; i < 1 + kChains; ++i) {
+    if constexpr (Op::kPack == 2) {
+      const uint32_t h = static_cast<const unsigned short*>(host)[i];
+      c.v[i] = h | (h << 16);
+    } else if constexpr (Op::kStorageBytes == 1) {
+      c.v[i] = static_cast<const int8_t*>(host)[i];
+    } else {
+      c.v[i] = static_cast<const typename Op::Word*>(host)[i];
+    }
+  }
+  return c;
+}
+
+// Launch one op's kernel: `imm_host` (host coefficients, by-value path) or
+// `coeff` (device coefficients).
+template <typename Op>
+int launch_op(int e, int u, const void* in, void* out, const void* coeff, const void* imm_host,
+              long long words, int iterations, int blocks, int threads, cudaStream_t s,
+              bool query_only, const void** fn_out) {
+  ChainFnT<Op> fn = imm_host != nullptr || query_only ? pick<Op, true>(e, u) : pick<Op, false>(e, u);
+  if (fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
+  if (fn_out != nullptr) *fn_out = reinterpret_cast<const void*>(fn);
+  if (query_only) return TCB_OK;
+  const CoeffImm<Op> imm = imm_host != nullptr ? host_coeffs<Op>(imm_host) : CoeffImm<Op>{};
+  clear_stale_error();
+  fn<<<blocks, threads, 0, s>>>(in, out, coeff, imm, words, iterations);
+  return launch_status();
+}
+
+struct OpFacts {
   int pack = 1;
   int storage_bytes = 4;
   const char* instruction = "";
 };
 
-Choice choose(int dtype, int e, int u) {
-  Choice c;
+// Dispatch on dtype: dtype facts, and (unless `facts_only`) the launch.
+int dispatch(int dtype, int e, int u, const void* in, void* out, const void* coeff,
+             const void* imm_host, long long words, int iterations, int blocks, int threads,
+             cudaStream_t s, bool query_only, const void** fn_out, OpFacts* facts,
+             bool facts_only) {
+#define TCB_VECTOR_CASE(CODE, OP)                                                           \
+  case CODE:                                                                                \
+    *facts = {OP::kPack, OP::kStorageBytes, OP::kInstruction};                              \
+    if (facts_only) return TCB_OK;                                                          \
+    return launch_op<OP>(e, u, in, out, coeff, imm_host, words, iterations, blocks, threads, \
+                         s, query_only, fn_out);
   switch (dtype) {
-    case TCB_V_BF16:
-      c = {pick<OpBF16>(e, u), 2, 2, OpBF16::kInstruction};
-      break;
-    case TCB_V_FP16:
-      c = {pick<OpFP16>(e, u), 2, 2, OpFP16::kInstruction};
-      break;
-    case TCB_V_FP32:
-      c = {pick<OpFP32>(e, u), 1, 4, OpFP32::kInstruction};
-      break;
-    case TCB_V_FP64:
-      c = {pick<OpFP64>(e, u), 1, 8, OpFP64::kInstruction};
-      break;
-    case TCB_V_INT8_DP4A:
-      c = {pick<OpDP4A>(e, u), 1, 4, OpDP4A::kInstruction};
-      break;
-    case TCB_V_INT32_IMAD:
-      c = {pick<OpIMAD>(e, u), 1, 4, OpIMAD::kInstruction};
-      break;
-    case TCB_V_INT8_MULADD:
-      c = {pick<OpI8MulAdd>(e, u), 1, 1, OpI8MulAdd::kInstruction};
-      break;
+    TCB_VECTOR_CASE(TCB_V_BF16, OpBF16)
+    TCB_VECTOR_CASE(TCB_V_FP16, OpFP16)
+    TCB_VECTOR_CASE(TCB_V_FP32, OpFP32)
+    TCB_VECTOR_CASE(TCB_V_FP64, OpFP64)
+    TCB_VECTOR_CASE(TCB_V_INT8_DP4A, OpDP4A)
+    TCB_VECTOR_CASE(TCB_V_INT32_IMAD, OpIMAD)
+    TCB_VECTOR_CASE(TCB_V_INT8_MULADD, OpI8MulAdd)
     default:
-      break;
+      return TCB_ERR_INVALID_ARGUMENT;
   }
-  return c;
+#undef TCB_VECTOR_CASE
 }
 
 }  // namespace
 
 int vector_kernel_info(int dtype, int threads, int elems_per_thread, int unroll,
                        tcb_kernel_info_t* out) {
-  Choice c = choose(dtype, elems_per_thread, unroll);
-  if (c.fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
+  OpFacts facts;
+  const void* fn = nullptr;
+  int rc = dispatch(dtype, elems_per_thread, unroll, nullptr, nullptr, nullptr, nullptr, 0, 0, 0,
+                    0, nullptr, true, &fn, &facts, false);
+  if (rc != TCB_OK || fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
   cudaFuncAttributes attr;
-  if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(c.fn)) != cudaSuccess)
-    return TCB_ERR_DEVICE;
+  if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
   out->dynamic_smem_bytes = 0;
   out->threads_per_block = threads;
   out->tensor_core = 0;
-  copy_str(out->instruction, sizeof(out->instruction), c.instruction);
+  copy_str(out->instruction, sizeof(out->instruction), facts.instruction);
   copy_str(out->execution_kind, sizeof(out->execution_kind), "simt");
   return TCB_OK;
 }
 
+namespace {
+
+int vector_launch(int dtype, const void* in, void* out, const void* coeff, const void* imm_host,
+                  long long elements, int iterations, int blocks, int threads,
+                  int elems_per_thread, int unroll, tcb_stream_t stream) {
+  if (in == nullptr || out == nullptr || (coeff == nullptr && imm_host == nullptr))
+    return TCB_ERR_INVALID_ARGUMENT;
+  if (iterations < 0 || blocks <= 0 || threads < 32 || threads > 1024 || threads % 32)
+    return TCB_ERR_INVALID_ARGUMENT;
+  if (elements != static_cast<long long>(blocks) * threads * elems_per_thread)
+    return TCB_ERR_INVALID_ARGUMENT;
+  OpFacts facts;
+  int rc = dispatch(dtype, elems_per_thread, unroll, nullptr, nullptr, nullptr, nullptr, 0, 0, 0,
+                    0, nullptr, false, nullptr, &facts, true);
+  if (rc != TCB_OK) return rc;
+  if (facts.pack == 2 && !(aligned(in, 4) && aligned(out, 4))) return TCB_ERR_ALIGNMENT;
+  if (!aligned(in, facts.storage_bytes * facts.pack) ||
+      !aligned(out, facts.storage_bytes * facts.pack))
+    return TCB_ERR_ALIGNMENT;
+  const long long words_per_chain = elements / facts.pack;
+  return dispatch(dtype, elems_per_thread, unroll, in, out, coeff, imm_host, words_per_chain,
+                  iterations, blocks, threads, reinterpret_cast<cudaStream_t>(stream), false,
+                  nullptr, &facts, false);
+}
+
+}  // namespace
 }  // namespace tcb
 
 using namespace tcb;
@@ -305,19 +380,16 @@ using namespace tcb;
 extern "C" int tcb_vector_chains(int dtype, const void* in, void* out, const void* coeff,
                                  long long elements, int iterations, int blocks, int threads,
                                  int elems_per_thread, int unroll, tcb_stream_t stream) {
-  if (in == nullptr || out == nullptr || coeff == nullptr) return TCB_ERR_INVALID_ARGUMENT;
-  if (iterations < 0 || blocks <= 0 || threads < 32 || threads > 1024 || threads % 32)
-    return TCB_ERR_INVALID_ARGUMENT;
-  Choice c = choose(dtype, elems_per_thread, unroll);
-  if (c.fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
-  if (elements != static_cast<long long>(blocks) * threads * elems_per_thread)
-    return TCB_ERR_INVALID_ARGUMENT;
-  if (c.pack == 2 && !(aligned(in, 4) && aligned(out, 4))) return TCB_ERR_ALIGNMENT;
-  if (!aligned(in, c.storage_bytes * c.pack) || !aligned(out, c.storage_bytes * c.pack))
-    return TCB_ERR_ALIGNMENT;
-  const long long words_per_chain = elements / c.pack;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  clear_stale_error();
-  c.fn<<<blocks, threads, 0, s>>>(in, out, coeff, words_per_chain, iterations);
-  return launch_status();
+  if (coeff == nullptr) return TCB_ERR_INVALID_ARGUMENT;
+  return vector_launch(dtype, in, out, coeff, nullptr, elements, iterations, blocks, threads,
+                       elems_per_thread, unroll, stream);
+}
+
+extern "C" int tcb_vector_chains_imm(int dtype, const void* in, void* out,
+                                     const void* coeff_host, long long elements, int iterations,
+                                     int blocks, int threads, int elems_per_thread, int unroll,
+                                     tcb_stream_t stream) {
+  if (coeff_host == nullptr) return TCB_ERR_INVALID_ARGUMENT;
+  return vector_launch(dtype, in, out, nullptr, coeff_host, elements, iterations, blocks, threads,
+                       elems_per_thread, unroll, stream);
 }
