@@ -9,7 +9,6 @@ if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
 GOLDEN = REPO / "tests" / "golden"
-REFERENCE = Path(os.environ.get("TCB_REFERENCE_ROOT", "/root/reference"))
 
 
 def pytest_configure(config):

@@ -3,7 +3,8 @@
 
 Imports the reference suite's own Python modules (bench_tensor, bench_vector,
 bench_bandwidth, suite_report, common) read-only from REFERENCE_ROOT
-(default /root/reference) and records what they compute or decide:
+(default: a `reference` checkout beside this repository) and records what they
+compute or decide:
 
   tensor.json / tensor_inputs.npz  E2M1 table and packing, tolerances, validate
                                    verdicts, operand sets and exact references
@@ -34,7 +35,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REFERENCE_ROOT = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+REFERENCE_ROOT = Path(os.environ.get("REFERENCE_ROOT", str(REPO.parent / "reference")))
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REPO / "tests"))
 sys.path.insert(0, str(REFERENCE_ROOT))
