@@ -294,7 +294,15 @@ using GemmFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 
 // MX FP4 uses 128 x 256 tiles (its scales need tensor-memory columns); the
 // other kinds use 256 x 256 unless M fits in one 128-row tile.
-int gemm_halves(int kind, int m) { return kind != gMXF4 && m > 128 ? 2 : 1; }
+// 256-row tiles halve the operand traffic per FLOP but also the tile count:
+// they are used only when there are at least as many of them as SMs, so a
+// 2048 x 2048 problem (64 such tiles) runs as 128 tiles of 128 x 256 instead of
+// leaving more than half the SMs idle.
+int gemm_halves(int kind, int m, int n, int sm_count) {
+  if (kind == gMXF4 || m <= 128) return 1;
+  const long long tiles256 = static_cast<long long>((m + 255) / 256) * ((n + kTileN - 1) / kTileN);
+  return tiles256 >= sm_count ? 2 : 1;
+}
 
 GemmFn gemm_fn(int kind, int halves) {
   if (halves == 2) {
@@ -429,7 +437,7 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
     copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
     return TCB_OK;
   }
-  const int halves = gemm_halves(kind, 256);
+  const int halves = gemm_halves(kind, 1 << 16, 1 << 16, 1);
   cudaFuncAttributes attr;
   if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind, halves))) !=
       cudaSuccess)
@@ -539,7 +547,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
     return gemm_pair_launch(map_a, map_b, map_c, args, pairs, facts,
                             reinterpret_cast<cudaStream_t>(stream));
   }
-  const int halves = gemm_halves(kind, M);
+  const int halves = gemm_halves(kind, M, N, facts.sm_count);
   const int tile_m = 128 * halves;
   CUtensorMap map_a, map_b;
   if ((rc = gemm_map(&map_a, A, M, kbytes, tile_m)) != TCB_OK) return rc;
