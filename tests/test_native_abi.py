@@ -77,3 +77,14 @@ def test_mx_scales_packed_bytes_matches_oracle(native):
         assert native.mx_scales_packed_bytes(rows, groups) == expected
     with pytest.raises(native.TcbError):
         native.mx_scales_packed_bytes(0, 8)
+
+
+def test_integration_binding_stub_matches_the_header():
+    """The reference-side ctypes stub compiles and names only declared entry points."""
+    text = (REPO / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```python\n(.*?)```", text, flags=re.S)
+    assert blocks
+    for block in blocks:
+        compile(block, "INTEGRATION.md", "exec")
+    used = set(re.findall(r"_lib\.(tcb_[a-z_0-9]+)", "\n".join(blocks)))
+    assert used and used <= set(declared_functions()), used - set(declared_functions())
