@@ -7,25 +7,33 @@
 namespace tcb {
 
 int current_device_facts(DeviceFacts* out) {
-  // Facts are cached per device ordinal; attribute queries are cheap but a
-  // launch path should not repeat them on every call.
-  static DeviceFacts cache[64];
+  // Facts are cached per device ordinal (attribute queries are cheap, but a
+  // launch path should not repeat them on every call); the first query of a
+  // device runs under a lock, later ones read the published copy.
+  constexpr int kMax = 64;
+  static DeviceFacts cache[kMax];
+  static std::atomic<bool> ready[kMax];
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return TCB_ERR_DEVICE;
-  if (dev < 0 || dev >= 64) return TCB_ERR_DEVICE;
-  DeviceFacts& f = cache[dev];
-  if (f.device != dev) {
-    DeviceFacts g;
-    g.device = dev;
-    if (cudaDeviceGetAttribute(&g.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&g.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
-            cudaSuccess ||
-        cudaDeviceGetAttribute(&g.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&g.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
-      return TCB_ERR_DEVICE;
-    f = g;
+  if (dev < 0 || dev >= kMax) return TCB_ERR_DEVICE;
+  if (!ready[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[dev].load(std::memory_order_relaxed)) {
+      DeviceFacts g;
+      g.device = dev;
+      if (cudaDeviceGetAttribute(&g.sm_count, cudaDevAttrMultiProcessorCount, dev) !=
+              cudaSuccess ||
+          cudaDeviceGetAttribute(&g.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                 dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&g.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&g.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+        return TCB_ERR_DEVICE;
+      cache[dev] = g;
+      ready[dev].store(true, std::memory_order_release);
+    }
   }
-  *out = f;
+  *out = cache[dev];
   return TCB_OK;
 }
 

@@ -271,11 +271,10 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
   const int stages = copy_bulk_stages(threads);
   if (stages < 2 || stages > kBulkMaxStages) return TCB_ERR_INVALID_ARGUMENT;
   const int smem = copy_bulk_smem_bytes(stages);
-  static int cap_device = -1, cap = 0;
-  if (cap_device != facts.device) {
-    cap = raise_dynamic_smem(reinterpret_cast<const void*>(copy_bulk_kernel), facts.max_smem_optin);
-    cap_device = facts.device;
-  }
+  static DeviceIntCache cap_cache;
+  const int cap = cap_cache.get(facts.device, [&] {
+    return raise_dynamic_smem(reinterpret_cast<const void*>(copy_bulk_kernel), facts.max_smem_optin);
+  });
   if (cap < smem) return TCB_ERR_RESOURCE;
   if (blocks == 0) blocks = facts.sm_count * 2;
   copy_bulk_kernel<<<blocks, 32, smem, s>>>(static_cast<const unsigned char*>(src),

@@ -366,15 +366,17 @@ uint32_t gemm_idesc(int kind, int mma_m = 128) {
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  // Resolved once (thread-safe static initialisation).
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     cudaDriverEntryPointQueryResult q;
     void* ptr = nullptr;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    clear_stale_error();
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
@@ -570,16 +572,11 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   args.idesc = gemm_idesc(kind);
   GemmFn fn = gemm_fn(kind, halves);
   const int smem = gemm_smem(kind, halves);
-  static int cap[6][2][64] = {};
-  if (facts.device >= 64) return TCB_ERR_DEVICE;
-  int& dev_cap = cap[kind][halves - 1][facts.device];
-  if (dev_cap == 0) {
-    dev_cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
-    if (dev_cap < smem) {
-      dev_cap = 0;
-      return TCB_ERR_RESOURCE;
-    }
-  }
+  static DeviceIntCache cap_cache[6][2];
+  const int cap = cap_cache[kind][halves - 1].get(facts.device, [&] {
+    return raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+  });
+  if (cap < smem) return TCB_ERR_RESOURCE;
   const int tiles = args.tiles_m * args.tiles_n;
   if (blocks == 0) blocks = facts.sm_count;
   if (blocks > tiles) blocks = tiles;

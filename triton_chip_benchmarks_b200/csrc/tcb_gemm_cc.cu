@@ -348,16 +348,11 @@ int gemm_cuda_core(int dtype, const void* A, const void* B, void* C, int M, int 
   DeviceFacts facts;
   int rc = current_device_facts(&facts);
   if (rc != TCB_OK) return rc;
-  static int cap[2][64] = {};
-  if (facts.device >= 64) return TCB_ERR_DEVICE;
-  int& dev_cap = cap[vec_in ? 1 : 0][facts.device];
-  if (dev_cap == 0) {
-    dev_cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
-    if (dev_cap < kDgSmem) {
-      dev_cap = 0;
-      return TCB_ERR_RESOURCE;
-    }
-  }
+  static DeviceIntCache cap_cache[2];
+  const int cap = cap_cache[vec_in ? 1 : 0].get(facts.device, [&] {
+    return raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+  });
+  if (cap < kDgSmem) return TCB_ERR_RESOURCE;
   fn<<<static_cast<int>(tiles), kCcThreads, kDgSmem, stream>>>(args);
   return launch_status();
 }

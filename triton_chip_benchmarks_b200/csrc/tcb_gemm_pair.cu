@@ -270,19 +270,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 int gemm_pair_launch(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_c,
                      const GemmArgs& args, int pairs, const DeviceFacts& facts,
                      cudaStream_t stream) {
-  static int cap[64] = {};
-  static int resident[64] = {};
-  if (facts.device < 0 || facts.device >= 64) return TCB_ERR_DEVICE;
-  int& dev_cap = cap[facts.device];
-  if (dev_cap == 0) {
-    dev_cap = raise_dynamic_smem(reinterpret_cast<const void*>(gemm_pair_mxf4_kernel),
-                                 facts.max_smem_optin);
-    if (dev_cap < kPairSmem) {
-      dev_cap = 0;
-      return TCB_ERR_RESOURCE;
-    }
-    // Pairs that can be resident at once: persistent pairs beyond that would
-    // only start when others finish, serialising their tiles.
+  static DeviceIntCache cap_cache, resident_cache;
+  const int cap = cap_cache.get(facts.device, [&] {
+    return raise_dynamic_smem(reinterpret_cast<const void*>(gemm_pair_mxf4_kernel),
+                              facts.max_smem_optin);
+  });
+  if (cap < kPairSmem) return TCB_ERR_RESOURCE;
+  // Pairs that can be resident at once: persistent pairs beyond that would
+  // only start when others finish, serialising their tiles.
+  const int resident = resident_cache.get(facts.device, [&] {
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(2 * (facts.sm_count / 2), 1, 1);
     config.blockDim = dim3(kPairThreads, 1, 1);
@@ -300,9 +296,9 @@ int gemm_pair_launch(const CUtensorMap& map_a, const CUtensorMap& map_b, const C
       clear_stale_error();
       clusters = facts.sm_count / 2;
     }
-    resident[facts.device] = clusters;
-  }
-  if (pairs > resident[facts.device]) pairs = resident[facts.device];
+    return clusters;
+  });
+  if (pairs > resident) pairs = resident;
   clear_stale_error();
   gemm_pair_mxf4_kernel<<<2 * pairs, kPairThreads, kPairSmem, stream>>>(map_a, map_b, map_c,
                                                                           args);

@@ -1,8 +1,12 @@
 // Host-side helpers shared by the launch entry points of libtcb.
 #pragma once
 
+#include <atomic>
+#include <climits>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
+
 #include <cuda_runtime.h>
 
 #include "tcb_status.h"
@@ -44,6 +48,35 @@ inline int raise_dynamic_smem(const void* fn, int max_optin) {
   }
   return cap;
 }
+
+// A per-device integer computed once (for example a kernel's dynamic
+// shared-memory allowance).  Thread-safe: the first caller for a device runs
+// `compute` under a lock, later callers read the published value.
+class DeviceIntCache {
+ public:
+  DeviceIntCache() {
+    for (auto& v : value_) v.store(kUnset, std::memory_order_relaxed);
+  }
+  template <typename F>
+  int get(int device, F compute) {
+    if (device < 0 || device >= kMaxDevices) return -1;
+    int v = value_[device].load(std::memory_order_acquire);
+    if (v != kUnset) return v;
+    std::lock_guard<std::mutex> lock(mu_);
+    v = value_[device].load(std::memory_order_relaxed);
+    if (v == kUnset) {
+      v = compute();
+      value_[device].store(v, std::memory_order_release);
+    }
+    return v;
+  }
+
+ private:
+  static constexpr int kMaxDevices = 64;
+  static constexpr int kUnset = INT_MIN;
+  std::atomic<int> value_[kMaxDevices];
+  std::mutex mu_;
+};
 
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

@@ -449,15 +449,17 @@ int make_plan(int dtype, int tile_m, int tile_n, int tile_k, int chains, int bps
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  // Resolved once (thread-safe static initialisation).
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
     cudaDriverEntryPointQueryResult q;
     void* ptr = nullptr;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    clear_stale_error();
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
@@ -522,17 +524,11 @@ int tc_tensor_peak(int dtype, const void* A, const void* B, const void* SA, cons
   KernelFn fn = kernel_for(p.kind, p.ksteps);
   if (fn == nullptr) return TCB_ERR_UNSUPPORTED;
   // Raise the dynamic shared-memory cap once per (kernel, device).
-  static int dyn_cap[6][6][64] = {};
-  if (facts.device >= 64) return TCB_ERR_DEVICE;
-  int& cap = dyn_cap[p.kind][steps_index(p.ksteps)][facts.device];
-  if (cap == 0) {
-    cap = raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
-    if (cap < 0) {
-      cap = 0;
-      return TCB_ERR_RESOURCE;
-    }
-  }
-  if (p.smem_bytes > cap) return TCB_ERR_RESOURCE;
+  static DeviceIntCache cap_cache[6][6];
+  const int cap = cap_cache[p.kind][steps_index(p.ksteps)].get(facts.device, [&] {
+    return raise_dynamic_smem(reinterpret_cast<const void*>(fn), facts.max_smem_optin);
+  });
+  if (cap < 0 || p.smem_bytes > cap) return TCB_ERR_RESOURCE;
   if (p.smem_request > cap) p.smem_request = cap;
   clear_stale_error();
   fn<<<blocks, kThreads, p.smem_request, stream>>>(map_a, map_b, args);
