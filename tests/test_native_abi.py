@@ -88,3 +88,35 @@ def test_integration_binding_stub_matches_the_header():
         compile(block, "INTEGRATION.md", "exec")
     used = set(re.findall(r"_lib\.(tcb_[a-z_0-9]+)", "\n".join(blocks)))
     assert used and used <= set(declared_functions()), used - set(declared_functions())
+
+
+def test_entry_points_reject_bad_arguments_before_touching_a_device(native):
+    """Argument validation returns a status without any CUDA call (runs without a GPU)."""
+    lib = native.load()
+    fake = 0x1000  # never dereferenced: every call below is rejected before a launch
+    # Zero bytes is a no-op; null buffers and unknown variants are invalid.
+    assert lib.tcb_copy(None, None, 0, native.COPY_BULK, 0, 0, None) == native.OK
+    assert lib.tcb_copy(None, fake, 64, native.COPY_BULK, 0, 0, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.tcb_copy(fake, fake, 64, 9, 0, 0, None) == native.ERR_INVALID_ARGUMENT
+    # Vector chains: elements must equal blocks x threads x elements per thread.
+    coeff = (ctypes.c_float * 9)()
+    for fn, c in ((lib.tcb_vector_chains, fake), (lib.tcb_vector_chains_imm,
+                                                    ctypes.addressof(coeff))):
+        assert fn(native.V_FP32, fake, fake, c, 1000, 4, 2, 128, 2, 4, None) == \
+            native.ERR_INVALID_ARGUMENT
+        assert fn(native.V_FP32, fake, fake, c, 512, 4, 2, 100, 2, 4, None) == \
+            native.ERR_INVALID_ARGUMENT
+    assert lib.tcb_vector_chains_imm(native.V_FP32, fake, fake, None, 512, 4, 2, 128, 2, 4,
+                                     None) == native.ERR_INVALID_ARGUMENT
+    # GEMM: a bf16 row of 60 elements is not a whole number of 16-byte TMA units.
+    assert lib.tcb_gemm(native.T_BF16, fake, fake, None, None, fake, 128, 128, 60, 0, None,
+                        None) == native.ERR_UNSUPPORTED
+    assert lib.tcb_gemm(native.T_BF16, None, fake, None, None, fake, 128, 128, 64, 0, None,
+                        None) == native.ERR_INVALID_ARGUMENT
+    assert lib.tcb_gemm(native.T_MXF4, fake, fake, None, None, fake, 256, 256, 256, 0, None,
+                        None) == native.ERR_INVALID_ARGUMENT  # MX FP4 needs its scales
+    assert lib.tcb_mx_scales_pack(None, fake, 128, 8, None) == native.ERR_INVALID_ARGUMENT
+    # Resident probe: at least one block and one iteration.
+    assert lib.tcb_tensor_peak(native.T_FP64, native.TV_DMMA, fake, fake, None, None, fake, 0, 1,
+                               128, 128, 16, 1, 1, None, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.tcb_kernel_info(99, 0, 0, 0, 0, 0, 0, 0, None) == native.ERR_INVALID_ARGUMENT
