@@ -6,9 +6,9 @@
 //     stored transposed (A^T, B^T) into double-buffered shared memory, so each
 //     thread reads its 8 rows / 8 columns of one k with two 16-byte loads.
 //   * FP64 on the double-precision MMA path (`mma.sync.m16n8k4.f64`): 128 x
-//     128 CTA tile, 8 warps of 32 x 64, K slabs of 16 streamed through a
+//     128 CTA tile, 8 warps of 32 x 64, K slabs of 32 streamed through a
 //     3-stage cp.async ring into padded row-major shared memory (row pitch
-//     20 doubles, so the fragment loads of a half-warp hit distinct banks).
+//     36 doubles, so the fragment loads of a half-warp hit distinct banks).
 //
 // A [M][K] and B [N][K] are K-contiguous, C [M][N] row-major (fp32 / fp64).
 // Any M, N, K: loads past an edge read zeros, stores are masked (the
@@ -163,8 +163,8 @@ __global__ void __launch_bounds__(kCcThreads, 2) sgemm_kernel(const CcArgs args)
 }
 
 // ------------------------------------------------------------------- FP64
-constexpr int kDgK = 16;       // K per slab (four m16n8k4 steps)
-constexpr int kDgPitch = 20;   // doubles per shared row
+constexpr int kDgK = 32;       // K per slab (eight m16n8k4 steps)
+constexpr int kDgPitch = 36;   // doubles per shared row (== 4 mod 16: conflict-free fragments)
 constexpr int kDgStages = 3;
 constexpr int kDgStageDoubles = 2 * kCcTile * kDgPitch;  // A and B rows of one slab
 constexpr int kDgSmem = kDgStages * kDgStageDoubles * 8;
