@@ -14,7 +14,7 @@ from oracle import tensor as oracle_tensor
 pytestmark = pytest.mark.gpu
 
 BF16, FP16, TF32, FP32, FP64, INT8, FP8, MXF4 = range(8)
-TCGEN05, DMMA, SIMT = 0, 1, 2
+TCGEN05, DMMA, SIMT, SIMT_REG = 0, 1, 2, 3
 STORAGE = {BF16: torch.bfloat16, FP16: torch.float16, TF32: torch.float32,
            FP32: torch.float32, FP64: torch.float64, INT8: torch.int8,
            FP8: torch.float8_e4m3fn}
@@ -148,6 +148,30 @@ def test_fp32_simt_exact(cuda, native, m, n, k, chains, iterations):
     _check(FP32, got, a, b, iterations)
 
 
+# Register-resident FP32: one k per lane, passes of 32 x (1024 / K) outputs, the
+# K partial sums added by a shuffle reduce-scatter; each supported K, pass counts
+# above one in both directions, odd pass counts.
+@pytest.mark.parametrize("m,n,k,chains", [(64, 64, 32, 2), (128, 128, 32, 2), (256, 256, 32, 1),
+                                          (96, 160, 32, 1), (64, 192, 16, 1), (96, 256, 8, 2)])
+@pytest.mark.parametrize("iterations", [1, 7])
+def test_fp32_simt_reg_exact(cuda, native, m, n, k, chains, iterations):
+    blocks = 3
+    a, b = _operands(FP32, blocks, chains, m, n, k, seed=n + k + iterations)
+    got = _run(native, cuda, FP32, SIMT_REG, a, b, m, n, k, chains, blocks, iterations)
+    _check(FP32, got, a, b, iterations)
+
+
+def test_fp32_simt_reg_rejects_unsupported_shapes(cuda, native):
+    a = torch.zeros((1, 64, 64), dtype=torch.float32, device=cuda)
+    c = torch.zeros((1, 1, 64, 64), device=cuda)
+    for (m, n, k, dtype) in [(64, 64, 64, FP32), (48, 64, 32, FP32), (64, 96, 16, FP32),
+                             (64, 64, 32, FP64)]:
+        with pytest.raises(native.TcbError) as info:
+            native.tensor_peak(dtype, SIMT_REG, a, a, c, blocks=1, blocks_per_sm=1, tile_m=m,
+                               tile_n=n, tile_k=k, chains=1, iterations=1)
+        assert info.value.is_capability
+
+
 def test_fp32_precision_probes(cuda):
     from triton_chip_benchmarks_b200 import bench_tensor
     ieee = bench_tensor.validate_fp32_precision(cuda, "ieee")
@@ -181,6 +205,9 @@ def test_kernel_info_reports_instruction(native, cuda):
     assert info["local_bytes_per_thread"] == 0
     simt = native.kernel_info(native.FAMILY_TENSOR, FP32, SIMT, 256, 256, 32, 1, 1)
     assert simt["instruction"] == "fma.rn.f32" and simt["execution_kind"] == "simt"
+    reg = native.kernel_info(native.FAMILY_TENSOR, FP32, SIMT_REG, 256, 256, 32, 1, 1)
+    assert reg["instruction"] == "fma.rn.f32" and reg["execution_kind"] == "simt"
+    assert reg["local_bytes_per_thread"] == 0 and reg["threads_per_block"] == 256
 
 
 GEMM_CASES = [(BF16, 256, 256, 64), (BF16, 512, 512, 1024), (FP16, 384, 512, 192),

@@ -69,6 +69,17 @@ def test_fp4_tiles_carry_whole_mx_groups(inputs):
         assert config["block_k"] % 2 == 0
 
 
+@pytest.mark.parametrize("inputs", ["reference", "baseline"])
+def test_fp32_register_resident_tiles_fit_the_kernel(inputs):
+    """One k per lane (K <= 32), passes of 32 x (1024 / K) outputs, 8 warps."""
+    configs = [c for c in bench_tensor.peak_configs("fp32", inputs) if c["kernel"] == "simt_reg"]
+    assert configs
+    for config in configs:
+        assert config["block_k"] in (8, 16, 32)
+        assert config["block_m"] % 32 == 0 and config["block_n"] % (1024 // config["block_k"]) == 0
+        assert config["num_warps"] == 8
+
+
 def test_peak_tolerance_stays_far_below_a_dropped_iteration():
     tolerance = validation.peak_tolerance("bf16", 32, 1024)
     assert tolerance * 64 < 1 / 256

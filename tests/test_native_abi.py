@@ -52,6 +52,7 @@ def test_enums_match_header(native):
     pairs = {"TCB_T_BF16": native.T_BF16, "TCB_T_MXF4": native.T_MXF4,
              "TCB_T_FP32": native.T_FP32, "TCB_V_INT8_DP4A": native.V_INT8_DP4A,
              "TCB_V_INT8_MULADD": native.V_INT8_MULADD, "TCB_TV_SIMT": native.TV_SIMT,
+             "TCB_TV_SIMT_REG": native.TV_SIMT_REG,
              "TCB_COPY_BULK": native.COPY_BULK, "TCB_READ_BF16": native.READ_BF16,
              "TCB_FAMILY_TENSOR": native.FAMILY_TENSOR}
     for name, value in pairs.items():

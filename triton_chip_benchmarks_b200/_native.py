@@ -31,7 +31,7 @@ READ_FP32, READ_FP16, READ_BF16 = 0, 1, 2
 V_BF16, V_FP16, V_FP32, V_FP64, V_INT8_DP4A, V_INT32_IMAD, V_INT8_MULADD = range(7)
 
 T_BF16, T_FP16, T_TF32, T_FP32, T_FP64, T_INT8, T_FP8E4M3, T_MXF4 = range(8)
-TV_TCGEN05, TV_DMMA, TV_SIMT = 0, 1, 2
+TV_TCGEN05, TV_DMMA, TV_SIMT, TV_SIMT_REG = 0, 1, 2, 3
 
 FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR, FAMILY_GEMM = 0, 1, 2, 3, 4
 

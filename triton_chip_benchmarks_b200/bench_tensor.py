@@ -47,7 +47,9 @@ NATIVE = {"bf16": _native.T_BF16, "fp16": _native.T_FP16, "tf32": _native.T_TF32
 STORAGE = {"bf16": torch.bfloat16, "fp16": torch.float16, "tf32": torch.float32,
            "fp32": torch.float32, "fp64": torch.float64, "int8": torch.int8,
            "fp8": torch.float8_e4m3fn, "fp4": torch.uint8}
-VARIANT_NAMES = {_native.TV_TCGEN05: "tcgen05", _native.TV_DMMA: "dmma", _native.TV_SIMT: "simt"}
+VARIANT_NAMES = {_native.TV_TCGEN05: "tcgen05", _native.TV_DMMA: "dmma", _native.TV_SIMT: "simt",
+                 _native.TV_SIMT_REG: "simt_reg"}
+VARIANTS = {name: variant for variant, name in VARIANT_NAMES.items()}
 # Relative tolerance of the baseline operand sets (exact results pass trivially).
 BASELINE_RTOL = {"bf16": 1e-3, "fp16": 1e-3, "tf32": 1e-3, "fp32": 1e-5, "fp64": 1e-12,
                  "int8": 0.0, "fp8": 0.0, "fp4": 0.0}
@@ -117,7 +119,9 @@ def peak_configs(key: str, inputs: str) -> list[dict]:
     chains = 1 if inputs == "baseline" else 2
     configs = []
     if key == "fp32":
-        tiles = [(_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256)]
+        tiles = [(_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256),
+                 (_native.TV_SIMT_REG, 64, 64), (_native.TV_SIMT_REG, 128, 128),
+                 (_native.TV_SIMT_REG, 256, 256)]
     elif key == "fp64":
         tiles = [(_native.TV_DMMA, 128, 128), (_native.TV_DMMA, 256, 256),
                  (_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256)]

@@ -2,10 +2,12 @@
 //   * FP64 on the double-precision MMA path: mma.sync.aligned.m16n8k4 .f64,
 //     operands staged once in shared memory in fragment order;
 //   * IEEE FP32 and FP64 on the SIMT path: register-blocked fma.rn.f32 /
-//     fma.rn.f64 outer products (B200 has no IEEE-FP32 tensor instruction).
-// Both keep A and B resident in shared memory and accumulate
-// C += A . B^T `iterations` times in registers; the CTA tile is covered by
-// consecutive register-sized passes, each receiving all iterations.
+//     fma.rn.f64 outer products (B200 has no IEEE-FP32 tensor instruction);
+//   * IEEE FP32 on the SIMT path with the operands held in registers.
+// All keep A and B resident on chip (shared memory, or registers for the
+// last) and accumulate C += A . B^T `iterations` times in registers; the CTA
+// tile is covered by consecutive register-sized passes, each receiving all
+// iterations.
 //
 // Counterpart in the reference suite: _tensor_peak_kernel
 // (bench_tensor.py:406-449) for the fp64 and IEEE-fp32 rows, whose Triton
@@ -135,6 +137,100 @@ __global__ void __launch_bounds__(kSimtThreads, sizeof(T) == 4 ? 2 : 1)
   }
 }
 
+// --------------------------------------------------- SIMT, register-resident
+// IEEE FP32 with the operands held in registers for the whole reissue loop.
+// Each lane owns one k of a 16 x 8 output tile, i.e. 16 A values, 8 B values
+// and 16 x 8 partial sums (152 live registers), and the K lanes of a group
+// share that tile, so one 256-thread pass covers 32 x (1024 / K) outputs.
+// The loop body is 128 fma.rn.f32 in serpentine order (row i left to right,
+// row i + 1 right to left): every FMA shares its A or its B register with the
+// one before it, the last FMA of an iteration shares B with the first of the
+// next, and an accumulator is reused only 128 FMAs later.  After the last
+// iteration the K partial sums are added by a butterfly all-reduce (a
+// reduce-scatter, with fewer shuffles, changed the loop's register assignment
+// and cost a quarter of the rate) and the group's first lane stores the tile.
+// A and B are staged once into shared memory; each pass copies its fragments
+// from there.
+constexpr int kRegThreads = 256;
+constexpr int kRegTm = 16, kRegTn = 8;  // output tile of one lane group
+constexpr int kRegPassM = 32;           // pass rows (two tile rows)
+
+template <int K>
+constexpr int reg_pass_n() {
+  return kRegThreads / K / (kRegPassM / kRegTm) * kRegTn;  // 1024 / K
+}
+
+// TM, TN > 0 fix the tile extents at compile time (0 takes them from the
+// arguments), as for the shared-memory kernel.
+template <int K, int TM = 0, int TN = 0>
+__global__ void __launch_bounds__(kRegThreads, 1) simt_reg_peak_kernel(const SimtArgs args) {
+  constexpr int kPassN = reg_pass_n<K>();
+  constexpr int kPitch = K + 4;  // shared row pitch in floats (16-byte multiple)
+  constexpr int kVecs = K / 4;   // 16-byte vectors per operand row
+  constexpr int kVals = kRegTm * kRegTn;
+  static_assert(K == 8 || K == 16 || K == 32, "one k per lane of a group within a warp");
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int M = TM > 0 ? TM : args.tile_m, N = TN > 0 ? TN : args.tile_n;
+  float* sA = reinterpret_cast<float*>(smem_raw);  // [M][kPitch]
+  float* sB = sA + M * kPitch;                     // [chains][N][kPitch]
+  const int blk = blockIdx.x;
+  const float4* gA = reinterpret_cast<const float4*>(static_cast<const float*>(args.a) +
+                                                     static_cast<size_t>(blk) * M * K);
+  for (int i = threadIdx.x; i < M * kVecs; i += kRegThreads)
+    *reinterpret_cast<float4*>(sA + (i / kVecs) * kPitch + 4 * (i % kVecs)) = gA[i];
+  for (int c = 0; c < args.chains; ++c) {
+    const float4* gB = reinterpret_cast<const float4*>(
+        static_cast<const float*>(args.b) + static_cast<size_t>(c * args.blocks + blk) * N * K);
+    float* sBc = sB + c * N * kPitch;
+    for (int i = threadIdx.x; i < N * kVecs; i += kRegThreads)
+      *reinterpret_cast<float4*>(sBc + (i / kVecs) * kPitch + 4 * (i % kVecs)) = gB[i];
+  }
+  __syncthreads();
+
+  const int lk = threadIdx.x % K;    // this lane's k
+  const int tile = threadIdx.x / K;  // output tile within the pass
+  const int tm = tile % (kRegPassM / kRegTm), tn = tile / (kRegPassM / kRegTm);
+  for (int c = 0; c < args.chains; ++c) {
+    const float* sBc = sB + c * N * kPitch;
+    float* gC = static_cast<float*>(args.c) + static_cast<size_t>(c * args.blocks + blk) * M * N;
+    for (int pm = 0; pm < M / kRegPassM; ++pm) {
+      for (int pn = 0; pn < N / kPassN; ++pn) {
+        const int row0 = pm * kRegPassM + tm * kRegTm, col0 = pn * kPassN + tn * kRegTn;
+        float a[kRegTm], b[kRegTn], acc[kVals];
+#pragma unroll
+        for (int i = 0; i < kRegTm; ++i) a[i] = sA[(row0 + i) * kPitch + lk];
+#pragma unroll
+        for (int j = 0; j < kRegTn; ++j) b[j] = sBc[(col0 + j) * kPitch + lk];
+#pragma unroll
+        for (int v = 0; v < kVals; ++v) acc[v] = 0.0f;
+#pragma unroll 1
+        for (int it = 0; it < args.iterations; ++it) {
+#pragma unroll
+          for (int i = 0; i < kRegTm; ++i)
+#pragma unroll
+            for (int jj = 0; jj < kRegTn; ++jj) {
+              const int j = (i & 1) ? kRegTn - 1 - jj : jj;
+              fma_rn<float>(acc[i * kRegTn + j], a[i], b[j]);
+            }
+        }
+        // Butterfly all-reduce over the K lanes, then the group's first lane
+        // stores the tile.
+#pragma unroll
+        for (int v = 0; v < kVals; ++v)
+#pragma unroll
+          for (int s = 1; s < K; s <<= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], s);
+        if (lk == 0) {
+#pragma unroll
+          for (int v = 0; v < kVals; v += 4)
+            *reinterpret_cast<float4*>(gC + static_cast<size_t>(row0 + v / kRegTn) * N + col0 +
+                                       v % kRegTn) =
+                make_float4(acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ DMMA
 // 8 warps; warp tile 32 x 64 = 2 (m16) x 8 (n8) mma.sync.m16n8k4 tiles.
 // Warps are arranged WM x WN (WN = min(N, 256) / 64), one pass covers
@@ -243,6 +339,14 @@ SimtFn simt_fn_tile(int m, int n) {
   return simt_peak_kernel<T, K>;
 }
 
+template <int K>
+SimtFn simt_reg_fn_tile(int m, int n) {
+  if (m == 64 && n == 64) return simt_reg_peak_kernel<K, 64, 64>;
+  if (m == 128 && n == 128) return simt_reg_peak_kernel<K, 128, 128>;
+  if (m == 256 && n == 256) return simt_reg_peak_kernel<K, 256, 256>;
+  return simt_reg_peak_kernel<K>;
+}
+
 template <typename T>
 SimtFn simt_fn_k(int k, int m, int n) {
   switch (k) {
@@ -283,7 +387,23 @@ int simt_plan(int dtype, int variant, int tile_m, int tile_n, int tile_k, int ch
               int max_smem, SimtPlan* out) {
   SimtPlan p;
   if (chains < 1 || chains > 2) return TCB_ERR_INVALID_ARGUMENT;
-  if (variant == TCB_TV_SIMT) {
+  if (variant == TCB_TV_SIMT_REG) {
+    if (dtype != TCB_T_FP32) return TCB_ERR_UNSUPPORTED;
+    int pass_n = 0;
+    switch (tile_k) {
+      case 8: p.fn = simt_reg_fn_tile<8>(tile_m, tile_n); pass_n = reg_pass_n<8>(); break;
+      case 16: p.fn = simt_reg_fn_tile<16>(tile_m, tile_n); pass_n = reg_pass_n<16>(); break;
+      case 32: p.fn = simt_reg_fn_tile<32>(tile_m, tile_n); pass_n = reg_pass_n<32>(); break;
+      default: return TCB_ERR_UNSUPPORTED;
+    }
+    if (tile_m < 1 || tile_n < 1 || tile_m % kRegPassM || tile_n % pass_n || tile_m > 512 ||
+        tile_n > 512)
+      return TCB_ERR_UNSUPPORTED;
+    p.threads = kRegThreads;
+    p.smem = (tile_m + chains * tile_n) * (tile_k + 4) * 4;
+    p.instruction = "fma.rn.f32";
+    p.tensor = false;
+  } else if (variant == TCB_TV_SIMT) {
     if (dtype != TCB_T_FP32 && dtype != TCB_T_FP64) return TCB_ERR_UNSUPPORTED;
     if (tile_m % 128 || tile_n % 128 || tile_m > 512 || tile_n > 512) return TCB_ERR_UNSUPPORTED;
     p.fn = simt_fn(dtype, tile_k, tile_m, tile_n);

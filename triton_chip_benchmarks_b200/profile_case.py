@@ -21,7 +21,7 @@ import json
 import torch
 
 from . import _native
-from .bench_tensor import NATIVE, STORAGE, launch, peak_inputs, reference_output
+from .bench_tensor import NATIVE, STORAGE, VARIANTS, launch, peak_inputs, reference_output
 from .bench_vector import make_inputs, native_dtype, validate
 from .validation import validate_relative
 
@@ -55,9 +55,8 @@ def case_copy(args) -> dict:
 
 def case_tensor(args) -> dict:
     m, n, k = (int(v) for v in args.tile.split("x"))
-    config = dict(block_m=m, block_n=n, block_k=k, chains=args.chains, variant={
-        "tcgen05": _native.TV_TCGEN05, "dmma": _native.TV_DMMA, "simt": _native.TV_SIMT}[
-        args.kernel])
+    config = dict(block_m=m, block_n=n, block_k=k, chains=args.chains,
+                  variant=VARIANTS[args.kernel])
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     blocks = sms * args.blocks_per_sm
     gen = torch.Generator().manual_seed(0)
@@ -140,7 +139,7 @@ def main(argv=None):
     p.add_argument("--launches", type=int, default=3)
     p = sub.add_parser("tensor")
     p.add_argument("--dtype", default="bf16", choices=sorted(NATIVE))
-    p.add_argument("--kernel", default="tcgen05", choices=("tcgen05", "dmma", "simt"))
+    p.add_argument("--kernel", default="tcgen05", choices=("tcgen05", "dmma", "simt", "simt_reg"))
     p.add_argument("--tile", default="256x256x64")
     p.add_argument("--chains", type=int, default=1)
     p.add_argument("--blocks-per-sm", type=int, default=1)

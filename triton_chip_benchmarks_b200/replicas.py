@@ -42,7 +42,8 @@ def build_parser():
     parser.add_argument("--mib", type=int, default=4096, help="copy: bytes per buffer in MiB")
     parser.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
     parser.add_argument("--dtype", default="bf16")
-    parser.add_argument("--kernel", choices=("tcgen05", "dmma", "simt"), default="tcgen05")
+    parser.add_argument("--kernel", choices=("tcgen05", "dmma", "simt", "simt_reg"),
+                        default="tcgen05")
     parser.add_argument("--tile", default="256x256x64")
     parser.add_argument("--chains", type=int, default=1)
     parser.add_argument("--blocks-per-sm", type=int, default=1)
@@ -93,11 +94,10 @@ def prepare(args):
             raise AssertionError("copy validation failed")
         return run, 2 * n, "GB/s", {"bytes": n, "variant": args.variant}
     if args.probe == "tensor":
-        from .bench_tensor import launch, peak_inputs, reference_output
+        from .bench_tensor import VARIANTS, launch, peak_inputs, reference_output
         from .validation import validate_relative
         m, n, k = (int(v) for v in args.tile.split("x"))
-        variant = {"tcgen05": _native.TV_TCGEN05, "dmma": _native.TV_DMMA,
-                   "simt": _native.TV_SIMT}[args.kernel]
+        variant = VARIANTS[args.kernel]
         config = dict(block_m=m, block_n=n, block_k=k, chains=args.chains, variant=variant)
         blocks = sms * args.blocks_per_sm
         gen = torch.Generator().manual_seed(args.rank)
