@@ -1,0 +1,57 @@
+"""The ctypes stub of INTEGRATION.md, executed against the built library (GPU).
+
+The stub is what a maintainer adds beside the reference's scripts.  Here its
+_launch_peak runs tile shapes from the reference's own sweep
+(_peak_configs, bench_tensor.py:491-578) on operands laid out the way the
+reference's _peak_inputs lays them out (bench_tensor.py:647-672: A
+[blocks, M, K], B [chains, blocks, K, N], ternary values / 16), and every
+result must equal iterations x (A . B) exactly.
+"""
+
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+REPO = Path(__file__).resolve().parents[1]
+LIBRARY = REPO / "triton_chip_benchmarks_b200" / "libtcb.so"
+PLACEHOLDER = "/path/to/triton_chip_benchmarks_b200/libtcb.so"
+
+
+@pytest.fixture(scope="module")
+def stub(cuda):
+    text = (REPO / "INTEGRATION.md").read_text()
+    block = re.findall(r"```python\n(.*?)```", text, flags=re.S)[0]
+    assert PLACEHOLDER in block
+    namespace = {}
+    exec(compile(block.replace(PLACEHOLDER, str(LIBRARY)), "INTEGRATION.md", "exec"), namespace)
+    return namespace
+
+
+# (dtype, dot_input_precision, block_m, block_n, block_k): the reference's IEEE FP32
+# tiles (bench_tensor.py:499-503), its FP64 tiles (:497-498) and the one tile of its
+# NVIDIA set that the tcgen05 kernel takes (:504-511, M = 128).
+CASES = [(torch.float32, "ieee", 32, 32, 32), (torch.float32, "ieee", 32, 64, 32),
+         (torch.float32, "ieee", 64, 32, 32), (torch.float32, "ieee", 64, 64, 32),
+         (torch.float64, None, 32, 32, 16), (torch.float64, None, 32, 64, 16),
+         (torch.bfloat16, None, 128, 64, 32), (torch.float32, "tf32", 128, 64, 32)]
+
+
+@pytest.mark.parametrize("dtype,precision,m,n,k", CASES)
+def test_stub_runs_reference_tiles_exactly(stub, cuda, dtype, precision, m, n, k):
+    blocks, chains, iterations = 3, 2, 5
+    gen = torch.Generator().manual_seed(m * n + k)
+    a = (torch.randint(-1, 2, (blocks, m, k), generator=gen).double() / 16).to(dtype)
+    b = (torch.randint(-1, 2, (chains, blocks, k, n), generator=gen).double() / 16).to(dtype)
+    out_dtype = torch.float64 if dtype == torch.float64 else torch.float32
+    c = torch.full((chains, blocks, m, n), float("nan"), dtype=out_dtype, device=cuda)
+    config = dict(block_m=m, block_n=n, block_k=k, num_warps=4, num_stages=1, chains=chains)
+    stub["_launch_peak"](a.to(cuda), b.to(cuda), c, iterations, config,
+                         dot_input_precision=precision)
+    torch.cuda.synchronize()
+    expected = iterations * np.matmul(a.double().numpy()[None], b.double().numpy())
+    assert np.array_equal(c.cpu().double().numpy(), expected)

@@ -161,11 +161,23 @@ def test_fp32_simt_reg_exact(cuda, native, m, n, k, chains, iterations):
     _check(FP32, got, a, b, iterations)
 
 
+# FP64 on the same kernel: 8 x 8 lane tiles, passes of 32 x (512 / K); the
+# reference's FP64 tiles (32 x 32 and 32 x 64 at K = 16) among them.
+@pytest.mark.parametrize("m,n,k,chains", [(32, 32, 16, 2), (32, 64, 16, 2), (64, 64, 32, 1),
+                                          (256, 256, 32, 2), (96, 128, 8, 1)])
+@pytest.mark.parametrize("iterations", [1, 6])
+def test_fp64_simt_reg_exact(cuda, native, m, n, k, chains, iterations):
+    blocks = 3
+    a, b = _operands(FP64, blocks, chains, m, n, k, seed=m + n + k + iterations)
+    got = _run(native, cuda, FP64, SIMT_REG, a, b, m, n, k, chains, blocks, iterations)
+    _check(FP64, got, a, b, iterations)
+
+
 def test_fp32_simt_reg_rejects_unsupported_shapes(cuda, native):
     a = torch.zeros((1, 64, 64), dtype=torch.float32, device=cuda)
     c = torch.zeros((1, 1, 64, 64), device=cuda)
     for (m, n, k, dtype) in [(64, 64, 64, FP32), (48, 64, 32, FP32), (64, 96, 16, FP32),
-                             (64, 64, 32, FP64)]:
+                             (32, 48, 16, FP64), (64, 64, 32, BF16)]:
         with pytest.raises(native.TcbError) as info:
             native.tensor_peak(dtype, SIMT_REG, a, a, c, blocks=1, blocks_per_sm=1, tile_m=m,
                                tile_n=n, tile_k=k, chains=1, iterations=1)
@@ -208,6 +220,9 @@ def test_kernel_info_reports_instruction(native, cuda):
     reg = native.kernel_info(native.FAMILY_TENSOR, FP32, SIMT_REG, 256, 256, 32, 1, 1)
     assert reg["instruction"] == "fma.rn.f32" and reg["execution_kind"] == "simt"
     assert reg["local_bytes_per_thread"] == 0 and reg["threads_per_block"] == 256
+    reg64 = native.kernel_info(native.FAMILY_TENSOR, FP64, SIMT_REG, 32, 64, 16, 2, 1)
+    assert reg64["instruction"] == "fma.rn.f64" and reg64["execution_kind"] == "simt"
+    assert reg64["local_bytes_per_thread"] == 0
 
 
 GEMM_CASES = [(BF16, 256, 256, 64), (BF16, 512, 512, 1024), (FP16, 384, 512, 192),

@@ -70,14 +70,26 @@ def test_fp4_tiles_carry_whole_mx_groups(inputs):
 
 
 @pytest.mark.parametrize("inputs", ["reference", "baseline"])
-def test_fp32_register_resident_tiles_fit_the_kernel(inputs):
-    """One k per lane (K <= 32), passes of 32 x (1024 / K) outputs, 8 warps."""
-    configs = [c for c in bench_tensor.peak_configs("fp32", inputs) if c["kernel"] == "simt_reg"]
+@pytest.mark.parametrize("key,pass_cols", [("fp32", 1024), ("fp64", 512)])
+def test_register_resident_tiles_fit_the_kernel(inputs, key, pass_cols):
+    """One k per lane (K <= 32), passes of 32 x (pass_cols / K) outputs, 8 warps."""
+    configs = [c for c in bench_tensor.peak_configs(key, inputs) if c["kernel"] == "simt_reg"]
     assert configs
     for config in configs:
         assert config["block_k"] in (8, 16, 32)
-        assert config["block_m"] % 32 == 0 and config["block_n"] % (1024 // config["block_k"]) == 0
+        assert config["block_m"] % 32 == 0
+        assert config["block_n"] % (pass_cols // config["block_k"]) == 0
         assert config["num_warps"] == 8
+
+
+def test_reference_mode_sweeps_the_reference_fp32_and_fp64_tiles():
+    """bench_tensor.py:497-503 of the reference: FP64 32x32 / 32x64 at K 16, IEEE
+    FP32 32x32 / 32x64 / 64x32 / 64x64 at K 32."""
+    shapes = {key: {(c["block_m"], c["block_n"], c["block_k"])
+                    for c in bench_tensor.peak_configs(key, "reference")}
+              for key in ("fp32", "fp64")}
+    assert {(32, 32, 16), (32, 64, 16)} <= shapes["fp64"]
+    assert {(32, 32, 32), (32, 64, 32), (64, 32, 32), (64, 64, 32)} <= shapes["fp32"]
 
 
 def test_peak_tolerance_stays_far_below_a_dropped_iteration():

@@ -122,9 +122,15 @@ def peak_configs(key: str, inputs: str) -> list[dict]:
         tiles = [(_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256),
                  (_native.TV_SIMT_REG, 64, 64), (_native.TV_SIMT_REG, 128, 128),
                  (_native.TV_SIMT_REG, 256, 256)]
+        if inputs == "reference":  # the reference's IEEE FP32 tiles, bench_tensor.py:499-503
+            tiles += [(_native.TV_SIMT_REG, 32, 32), (_native.TV_SIMT_REG, 32, 64),
+                      (_native.TV_SIMT_REG, 64, 32)]
     elif key == "fp64":
         tiles = [(_native.TV_DMMA, 128, 128), (_native.TV_DMMA, 256, 256),
-                 (_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256)]
+                 (_native.TV_SIMT, 128, 128), (_native.TV_SIMT, 256, 256),
+                 (_native.TV_SIMT_REG, 64, 64), (_native.TV_SIMT_REG, 256, 256)]
+        if inputs == "reference":  # the reference's FP64 tiles, bench_tensor.py:497-498
+            tiles += [(_native.TV_SIMT_REG, 32, 32), (_native.TV_SIMT_REG, 32, 64)]
     else:
         tiles = [(_native.TV_TCGEN05, 128, 128), (_native.TV_TCGEN05, 128, 256),
                  (_native.TV_TCGEN05, 256, 256)]

@@ -138,79 +138,87 @@ __global__ void __launch_bounds__(kSimtThreads, sizeof(T) == 4 ? 2 : 1)
 }
 
 // --------------------------------------------------- SIMT, register-resident
-// IEEE FP32 with the operands held in registers for the whole reissue loop.
-// Each lane owns one k of a 16 x 8 output tile, i.e. 16 A values, 8 B values
-// and 16 x 8 partial sums (152 live registers), and the K lanes of a group
-// share that tile, so one 256-thread pass covers 32 x (1024 / K) outputs.
-// The loop body is 128 fma.rn.f32 in serpentine order (row i left to right,
-// row i + 1 right to left): every FMA shares its A or its B register with the
-// one before it, the last FMA of an iteration shares B with the first of the
-// next, and an accumulator is reused only 128 FMAs later.  After the last
-// iteration the K partial sums are added by a butterfly all-reduce (a
-// reduce-scatter, with fewer shuffles, changed the loop's register assignment
-// and cost a quarter of the rate) and the group's first lane stores the tile.
-// A and B are staged once into shared memory; each pass copies its fragments
-// from there.
+// IEEE FP32 (and FP64) with the operands held in registers for the whole
+// reissue loop.  Each lane owns one k of a 16 x 8 output tile (8 x 8 for
+// FP64), i.e. 16 A values, 8 B values and 16 x 8 partial sums (152 live
+// registers; FP64 8 + 8 + 64 doubles, 160), and the K lanes of a group share
+// that tile, so one 256-thread pass covers 32 x (1024 / K) outputs (FP64:
+// 32 x (512 / K)).  The loop body is 128 fma.rn.f32 (64 fma.rn.f64) in
+// serpentine order (row i left to right, row i + 1 right to left): every FMA
+// shares its A or its B register with the one before it, the last FMA of an
+// iteration shares B with the first of the next, and an accumulator is reused
+// only a whole tile of FMAs later.  After the last iteration the K partial
+// sums are added by a butterfly all-reduce (a reduce-scatter, with fewer
+// shuffles, changed the loop's register assignment and cost a quarter of the
+// rate) and the group's first lane stores the tile.  A and B are staged once
+// into shared memory; each pass copies its fragments from there.
 constexpr int kRegThreads = 256;
-constexpr int kRegTm = 16, kRegTn = 8;  // output tile of one lane group
-constexpr int kRegPassM = 32;           // pass rows (two tile rows)
+constexpr int kRegPassM = 32;  // pass rows
 
-template <int K>
+template <typename T>
+struct RegTile {                                        // output tile of one lane group
+  static constexpr int kRows = sizeof(T) == 4 ? 16 : 8;
+  static constexpr int kCols = 8;
+};
+
+template <typename T, int K>
 constexpr int reg_pass_n() {
-  return kRegThreads / K / (kRegPassM / kRegTm) * kRegTn;  // 1024 / K
+  return kRegThreads / K / (kRegPassM / RegTile<T>::kRows) * RegTile<T>::kCols;
 }
 
 // TM, TN > 0 fix the tile extents at compile time (0 takes them from the
 // arguments), as for the shared-memory kernel.
-template <int K, int TM = 0, int TN = 0>
+template <typename T, int K, int TM = 0, int TN = 0>
 __global__ void __launch_bounds__(kRegThreads, 1) simt_reg_peak_kernel(const SimtArgs args) {
-  constexpr int kPassN = reg_pass_n<K>();
-  constexpr int kPitch = K + 4;  // shared row pitch in floats (16-byte multiple)
-  constexpr int kVecs = K / 4;   // 16-byte vectors per operand row
-  constexpr int kVals = kRegTm * kRegTn;
+  constexpr int kRows = RegTile<T>::kRows, kCols = RegTile<T>::kCols;
+  constexpr int kPassN = reg_pass_n<T, K>();
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
+  constexpr int kPitch = K + kVec;      // shared row pitch in elements (16-byte multiple)
+  constexpr int kVecs = K / kVec;       // 16-byte vectors per operand row
+  constexpr int kVals = kRows * kCols;
   static_assert(K == 8 || K == 16 || K == 32, "one k per lane of a group within a warp");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int M = TM > 0 ? TM : args.tile_m, N = TN > 0 ? TN : args.tile_n;
-  float* sA = reinterpret_cast<float*>(smem_raw);  // [M][kPitch]
-  float* sB = sA + M * kPitch;                     // [chains][N][kPitch]
+  T* sA = reinterpret_cast<T*>(smem_raw);  // [M][kPitch]
+  T* sB = sA + M * kPitch;                 // [chains][N][kPitch]
   const int blk = blockIdx.x;
-  const float4* gA = reinterpret_cast<const float4*>(static_cast<const float*>(args.a) +
-                                                     static_cast<size_t>(blk) * M * K);
+  const uint4* gA = reinterpret_cast<const uint4*>(static_cast<const T*>(args.a) +
+                                                   static_cast<size_t>(blk) * M * K);
   for (int i = threadIdx.x; i < M * kVecs; i += kRegThreads)
-    *reinterpret_cast<float4*>(sA + (i / kVecs) * kPitch + 4 * (i % kVecs)) = gA[i];
+    *reinterpret_cast<uint4*>(sA + (i / kVecs) * kPitch + kVec * (i % kVecs)) = gA[i];
   for (int c = 0; c < args.chains; ++c) {
-    const float4* gB = reinterpret_cast<const float4*>(
-        static_cast<const float*>(args.b) + static_cast<size_t>(c * args.blocks + blk) * N * K);
-    float* sBc = sB + c * N * kPitch;
+    const uint4* gB = reinterpret_cast<const uint4*>(
+        static_cast<const T*>(args.b) + static_cast<size_t>(c * args.blocks + blk) * N * K);
+    T* sBc = sB + c * N * kPitch;
     for (int i = threadIdx.x; i < N * kVecs; i += kRegThreads)
-      *reinterpret_cast<float4*>(sBc + (i / kVecs) * kPitch + 4 * (i % kVecs)) = gB[i];
+      *reinterpret_cast<uint4*>(sBc + (i / kVecs) * kPitch + kVec * (i % kVecs)) = gB[i];
   }
   __syncthreads();
 
   const int lk = threadIdx.x % K;    // this lane's k
   const int tile = threadIdx.x / K;  // output tile within the pass
-  const int tm = tile % (kRegPassM / kRegTm), tn = tile / (kRegPassM / kRegTm);
+  const int tm = tile % (kRegPassM / kRows), tn = tile / (kRegPassM / kRows);
   for (int c = 0; c < args.chains; ++c) {
-    const float* sBc = sB + c * N * kPitch;
-    float* gC = static_cast<float*>(args.c) + static_cast<size_t>(c * args.blocks + blk) * M * N;
+    const T* sBc = sB + c * N * kPitch;
+    T* gC = static_cast<T*>(args.c) + static_cast<size_t>(c * args.blocks + blk) * M * N;
     for (int pm = 0; pm < M / kRegPassM; ++pm) {
       for (int pn = 0; pn < N / kPassN; ++pn) {
-        const int row0 = pm * kRegPassM + tm * kRegTm, col0 = pn * kPassN + tn * kRegTn;
-        float a[kRegTm], b[kRegTn], acc[kVals];
+        const int row0 = pm * kRegPassM + tm * kRows, col0 = pn * kPassN + tn * kCols;
+        T a[kRows], b[kCols], acc[kVals];
 #pragma unroll
-        for (int i = 0; i < kRegTm; ++i) a[i] = sA[(row0 + i) * kPitch + lk];
+        for (int i = 0; i < kRows; ++i) a[i] = sA[(row0 + i) * kPitch + lk];
 #pragma unroll
-        for (int j = 0; j < kRegTn; ++j) b[j] = sBc[(col0 + j) * kPitch + lk];
+        for (int j = 0; j < kCols; ++j) b[j] = sBc[(col0 + j) * kPitch + lk];
 #pragma unroll
-        for (int v = 0; v < kVals; ++v) acc[v] = 0.0f;
+        for (int v = 0; v < kVals; ++v) acc[v] = T(0);
 #pragma unroll 1
         for (int it = 0; it < args.iterations; ++it) {
 #pragma unroll
-          for (int i = 0; i < kRegTm; ++i)
+          for (int i = 0; i < kRows; ++i)
 #pragma unroll
-            for (int jj = 0; jj < kRegTn; ++jj) {
-              const int j = (i & 1) ? kRegTn - 1 - jj : jj;
-              fma_rn<float>(acc[i * kRegTn + j], a[i], b[j]);
+            for (int jj = 0; jj < kCols; ++jj) {
+              const int j = (i & 1) ? kCols - 1 - jj : jj;
+              fma_rn<T>(acc[i * kCols + j], a[i], b[j]);
             }
         }
         // Butterfly all-reduce over the K lanes, then the group's first lane
@@ -221,10 +229,14 @@ __global__ void __launch_bounds__(kRegThreads, 1) simt_reg_peak_kernel(const Sim
           for (int s = 1; s < K; s <<= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], s);
         if (lk == 0) {
 #pragma unroll
-          for (int v = 0; v < kVals; v += 4)
-            *reinterpret_cast<float4*>(gC + static_cast<size_t>(row0 + v / kRegTn) * N + col0 +
-                                       v % kRegTn) =
-                make_float4(acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
+          for (int v = 0; v < kVals; v += kVec) {
+            T* dst = gC + static_cast<size_t>(row0 + v / kCols) * N + col0 + v % kCols;
+            if constexpr (sizeof(T) == 4)
+              *reinterpret_cast<float4*>(dst) =
+                  make_float4(acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
+            else
+              *reinterpret_cast<double2*>(dst) = make_double2(acc[v], acc[v + 1]);
+          }
         }
       }
     }
@@ -339,12 +351,23 @@ SimtFn simt_fn_tile(int m, int n) {
   return simt_peak_kernel<T, K>;
 }
 
-template <int K>
+template <typename T, int K>
 SimtFn simt_reg_fn_tile(int m, int n) {
-  if (m == 64 && n == 64) return simt_reg_peak_kernel<K, 64, 64>;
-  if (m == 128 && n == 128) return simt_reg_peak_kernel<K, 128, 128>;
-  if (m == 256 && n == 256) return simt_reg_peak_kernel<K, 256, 256>;
-  return simt_reg_peak_kernel<K>;
+  if (m == 64 && n == 64) return simt_reg_peak_kernel<T, K, 64, 64>;
+  if (m == 128 && n == 128) return simt_reg_peak_kernel<T, K, 128, 128>;
+  if (m == 256 && n == 256) return simt_reg_peak_kernel<T, K, 256, 256>;
+  return simt_reg_peak_kernel<T, K>;
+}
+
+// (kernel, pass columns) of the register-resident kernel; nullptr for an unsupported K.
+template <typename T>
+SimtFn simt_reg_fn(int k, int m, int n, int* pass_n) {
+  switch (k) {
+    case 8: *pass_n = reg_pass_n<T, 8>(); return simt_reg_fn_tile<T, 8>(m, n);
+    case 16: *pass_n = reg_pass_n<T, 16>(); return simt_reg_fn_tile<T, 16>(m, n);
+    case 32: *pass_n = reg_pass_n<T, 32>(); return simt_reg_fn_tile<T, 32>(m, n);
+  }
+  return nullptr;
 }
 
 template <typename T>
@@ -388,20 +411,18 @@ int simt_plan(int dtype, int variant, int tile_m, int tile_n, int tile_k, int ch
   SimtPlan p;
   if (chains < 1 || chains > 2) return TCB_ERR_INVALID_ARGUMENT;
   if (variant == TCB_TV_SIMT_REG) {
-    if (dtype != TCB_T_FP32) return TCB_ERR_UNSUPPORTED;
+    if (dtype != TCB_T_FP32 && dtype != TCB_T_FP64) return TCB_ERR_UNSUPPORTED;
     int pass_n = 0;
-    switch (tile_k) {
-      case 8: p.fn = simt_reg_fn_tile<8>(tile_m, tile_n); pass_n = reg_pass_n<8>(); break;
-      case 16: p.fn = simt_reg_fn_tile<16>(tile_m, tile_n); pass_n = reg_pass_n<16>(); break;
-      case 32: p.fn = simt_reg_fn_tile<32>(tile_m, tile_n); pass_n = reg_pass_n<32>(); break;
-      default: return TCB_ERR_UNSUPPORTED;
-    }
+    p.fn = dtype == TCB_T_FP32 ? simt_reg_fn<float>(tile_k, tile_m, tile_n, &pass_n)
+                               : simt_reg_fn<double>(tile_k, tile_m, tile_n, &pass_n);
+    if (p.fn == nullptr) return TCB_ERR_UNSUPPORTED;
     if (tile_m < 1 || tile_n < 1 || tile_m % kRegPassM || tile_n % pass_n || tile_m > 512 ||
         tile_n > 512)
       return TCB_ERR_UNSUPPORTED;
+    const int es = dtype == TCB_T_FP32 ? 4 : 8;
     p.threads = kRegThreads;
-    p.smem = (tile_m + chains * tile_n) * (tile_k + 4) * 4;
-    p.instruction = "fma.rn.f32";
+    p.smem = (tile_m + chains * tile_n) * (tile_k + 16 / es) * es;
+    p.instruction = dtype == TCB_T_FP32 ? "fma.rn.f32" : "fma.rn.f64";
     p.tensor = false;
   } else if (variant == TCB_TV_SIMT) {
     if (dtype != TCB_T_FP32 && dtype != TCB_T_FP64) return TCB_ERR_UNSUPPORTED;
