@@ -194,7 +194,24 @@ def tensor_fixtures():
             ref_tensor._launch_peak = saved
         fp64.append({"answer": answer, "accepted": ok})
     out["fp64_probe_verdicts"] = fp64
+    out["status_classification"] = status_classification()
     (HERE / "tensor.json").write_text(json.dumps(out, indent=1) + "\n")
+
+
+def status_classification():
+    """The reference's verdict on each libtcb status message raised as RuntimeError.
+
+    _unsupported_reason (bench_tensor.py:94-142) decides whether a failed tile
+    is recorded as unsupported (non-null) or re-raised and ends the sweep (null).
+    """
+    from triton_chip_benchmarks_b200 import _native
+    lib = _native.load()
+    rows = []
+    for status in range(-1, -8, -1):
+        message = lib.tcb_strerror(status).decode()
+        rows.append({"status": status, "message": message,
+                     "reason": ref_tensor._unsupported_reason(RuntimeError(message))})
+    return rows
 
 
 # ------------------------------------------------------------------ vector

@@ -190,3 +190,16 @@ def test_gemm_inputs_pad_unaligned_k():
     assert not a[:, 1000:].any() and not b[:, 1000:].any()
     a, b, _ = gemm_inputs("bf16", 4, 3, 1000, torch.device("cpu"), gen)
     assert a.shape == (4, 1000)
+
+
+def test_status_messages_keep_the_reference_classification(native):
+    """The library's status messages are the ones the fixture recorded, and the
+    reference's _unsupported_reason (bench_tensor.py:94-142) accepts exactly
+    TCB_ERR_UNSUPPORTED's as a capability rejection: its sweep records such a tile
+    as unsupported and goes on, while every other failure is re-raised."""
+    lib = native.load()
+    rows = G["status_classification"]
+    assert {row["status"] for row in rows} == set(range(-7, 0))
+    for row in rows:
+        assert lib.tcb_strerror(row["status"]).decode() == row["message"]
+        assert (row["reason"] is not None) == (row["status"] == native.ERR_UNSUPPORTED)

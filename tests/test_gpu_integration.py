@@ -55,3 +55,15 @@ def test_stub_runs_reference_tiles_exactly(stub, cuda, dtype, precision, m, n, k
     torch.cuda.synchronize()
     expected = iterations * np.matmul(a.double().numpy()[None], b.double().numpy())
     assert np.array_equal(c.cpu().double().numpy(), expected)
+
+
+def test_stub_raises_reference_classifiable_rejection(stub, cuda):
+    """A 64-row tile of a tcgen05 kind (the reference's NVIDIA set) is rejected with
+    the message the reference's _unsupported_reason accepts (tests/golden/tensor.json,
+    status_classification), so the reference's sweep records it and goes on."""
+    a = torch.zeros((1, 64, 32), dtype=torch.bfloat16, device=cuda)
+    b = torch.zeros((2, 1, 32, 64), dtype=torch.bfloat16, device=cuda)
+    c = torch.zeros((2, 1, 64, 64), device=cuda)
+    config = dict(block_m=64, block_n=64, block_k=32, num_warps=4, num_stages=1, chains=2)
+    with pytest.raises(RuntimeError, match="unsupported matrix format or tile"):
+        stub["_launch_peak"](a, b, c, 1, config)

