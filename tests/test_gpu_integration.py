@@ -67,3 +67,49 @@ def test_stub_raises_reference_classifiable_rejection(stub, cuda):
     config = dict(block_m=64, block_n=64, block_k=32, num_warps=4, num_stages=1, chains=2)
     with pytest.raises(RuntimeError, match="unsupported matrix format or tile"):
         stub["_launch_peak"](a, b, c, 1, config)
+
+
+# (dtype, int8 operation, BLOCK_SIZE, num_warps) from the reference's NVIDIA vector
+# sweep (BLOCK 256-2048, warps 4 or 8): 256 elements over 8 warps is one element per
+# thread, which the stub runs on packed pairs for the 16-bit types.
+VECTOR_CASES = [("fp32", "dp4a", 1024, 4), ("fp64", "dp4a", 512, 8), ("bf16", "dp4a", 256, 8),
+                ("fp16", "dp4a", 256, 4), ("fp16", "dp4a", 2048, 8), ("int8", "dp4a", 2048, 8),
+                ("int8", "muladd", 512, 4)]
+
+
+@pytest.mark.parametrize("dtype,int8_op,block_size,num_warps", VECTOR_CASES)
+def test_stub_launch_vector_called_as_the_reference_calls_it(stub, cuda, dtype, int8_op,
+                                                             block_size, num_warps):
+    from types import SimpleNamespace
+
+    from triton_chip_benchmarks_b200 import bench_vector
+    args = SimpleNamespace(dtype=dtype, inputs="reference", seed=3, int8_op=int8_op)
+    blocks, iterations, unroll = 3, 64, 4
+    elements = blocks * block_size
+    inputs, coeff = bench_vector.make_inputs(args, elements, cuda)
+    output = torch.empty_like(inputs)
+    is_int8 = dtype == "int8"
+    use_dp4a = is_int8 and int8_op == "dp4a"
+    # The reference's positional call, bench_vector.py:1411-1416 (kernel object unused).
+    stub["launch_vector"](None, (blocks,), inputs, output, coeff, elements, iterations,
+                          block_size, unroll, True, num_warps, is_int8, use_dp4a, False, False,
+                          False, False)
+    torch.cuda.synchronize()
+    bench_vector.validate(args, inputs, output, coeff, iterations)  # raises on a mismatch
+
+
+def test_stub_copy_and_read_called_as_the_reference_calls_them(stub, cuda):
+    """launch_copy / launch_read with the reference's arguments (bench_bandwidth.py:
+    43-67), on an element count that fills neither a block nor a 16-byte vector."""
+    n = 4096 * 3 + 17
+    src = torch.randn(n, device=cuda)
+    dst = torch.full_like(src, float("nan"))
+    stub["launch_copy"](src, dst, 4096, 4)
+    block = 1024
+    sink = torch.full((-(-n // block),), float("nan"), device=cuda)
+    stub["launch_read"](src, sink, block, 8, "nvidia")
+    torch.cuda.synchronize()
+    assert torch.equal(src, dst)
+    expected = torch.nn.functional.pad(src.double(), (0, sink.numel() * block - n))
+    expected = expected.view(-1, block).sum(1)
+    assert torch.allclose(sink.double(), expected, rtol=1e-5, atol=1e-3)
