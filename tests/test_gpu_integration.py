@@ -113,3 +113,38 @@ def test_stub_copy_and_read_called_as_the_reference_calls_them(stub, cuda):
     expected = torch.nn.functional.pad(src.double(), (0, sink.numel() * block - n))
     expected = expected.view(-1, block).sum(1)
     assert torch.allclose(sink.double(), expected, rtol=1e-5, atol=1e-3)
+
+
+# (dtype, dot_input_precision, M, N, K) in GEMM mode, operands as the reference's
+# _inputs builds them (bench_tensor.py:249-261: randn A, randn B / sqrt(K), ternary
+# int8), B [K, N] row-major; tolerances of the reference's _validate (:289-299).
+GEMM_CASES = [(torch.bfloat16, None, 256, 256, 256, 2e-3), (torch.float16, None, 192, 320, 64, 2e-3),
+              (torch.float32, "tf32", 256, 128, 128, 1e-2), (torch.float32, "ieee", 200, 136, 72, 2e-3),
+              (torch.float64, None, 96, 160, 48, 1e-10), (torch.int8, None, 256, 256, 128, 0.0)]
+
+
+@pytest.mark.parametrize("dtype,precision,m,n,k,tol", GEMM_CASES)
+def test_stub_gemm_launch_as_the_reference_calls_it(stub, cuda, dtype, precision, m, n, k, tol):
+    gen = torch.Generator().manual_seed(m + n + k)
+    if dtype == torch.int8:
+        a = torch.randint(-1, 2, (m, k), generator=gen, dtype=dtype)
+        b = torch.randint(-1, 2, (k, n), generator=gen, dtype=dtype)
+        out_dtype = torch.int32
+    else:
+        wide = torch.float64 if dtype == torch.float64 else torch.float32
+        a = torch.randn((m, k), generator=gen, dtype=wide).to(dtype)
+        b = (torch.randn((k, n), generator=gen, dtype=wide) / k ** 0.5).to(dtype)
+        out_dtype = torch.float64 if dtype == torch.float64 else torch.float32
+    c = torch.empty((m, n), dtype=out_dtype, device=cuda)
+    config = dict(block_m=128, block_n=128, block_k=64, num_warps=4, num_stages=3)
+    a_dev, b_dev = a.to(cuda), b.to(cuda)
+    for _ in range(2):  # the second call uses the stub's cached K-contiguous B
+        c.fill_(0)
+        stub["_launch"](a_dev, b_dev, c, config, precision)
+        torch.cuda.synchronize()
+        expected = a.double() @ b.double()
+        got = c.cpu().double()
+        if tol == 0.0:
+            assert torch.equal(got, expected)
+        else:
+            assert torch.allclose(got, expected, rtol=tol, atol=tol)

@@ -91,6 +91,36 @@ def test_integration_binding_stub_matches_the_header():
     assert used and used <= set(declared_functions()), used - set(declared_functions())
 
 
+def test_integration_stub_derives_once_per_tensor_not_per_address(native):
+    """The stub's _once cache (host coefficients, K-contiguous B) follows the tensor
+    object: reused while the tensor lives unchanged, rebuilt after an in-place change,
+    and dropped with the tensor, so a new tensor at a recycled address never sees a
+    stale entry.  Executes the stub against the built library (no device needed)."""
+    import torch
+    text = (REPO / "INTEGRATION.md").read_text()
+    block = re.findall(r"```python\n(.*?)```", text, flags=re.S)[0]
+    namespace = {}
+    exec(compile(block.replace("/path/to/triton_chip_benchmarks_b200/libtcb.so",
+                               str(native.LIBRARY_PATH)),
+                 "INTEGRATION.md", "exec"), namespace)
+    once, derived = namespace["_once"], namespace["_derived"]
+    calls = []
+
+    def make(t):
+        calls.append(1)
+        return t.clone()
+
+    t = torch.arange(8.0)
+    first = once(t, make)
+    assert once(t, make) is first and len(calls) == 1
+    t.add_(1)
+    assert torch.equal(once(t, make), t) and len(calls) == 2
+    del t, first
+    assert not derived
+    u = torch.arange(8.0)
+    assert torch.equal(once(u, make), u) and len(calls) == 3 and len(derived) == 1
+
+
 def test_entry_points_reject_bad_arguments_before_touching_a_device(native):
     """Argument validation returns a status without any CUDA call (runs without a GPU)."""
     lib = native.load()
