@@ -137,8 +137,9 @@ int tcb_vector_chains_imm(int dtype, const void *in, void *out, const void *coef
 #define TCB_TV_TCGEN05 0  /* tcgen05.mma, accumulators in tensor memory */
 #define TCB_TV_DMMA 1     /* mma.sync f64 (fp64 only) */
 #define TCB_TV_SIMT 2     /* scalar FFMA / DFMA (fp32, fp64), operands read from shared memory */
-#define TCB_TV_SIMT_REG 3 /* scalar FFMA (fp32), operands held in registers; tile_k 8, 16
-                           * or 32, tile_m a multiple of 32, tile_n of 1024 / tile_k */
+#define TCB_TV_SIMT_REG 3 /* scalar FFMA / DFMA (fp32, fp64), operands held in registers;
+                           * tile_k 8, 16 or 32, tile_m a multiple of 32, tile_n a
+                           * multiple of 1024 / tile_k (fp32) or 512 / tile_k (fp64) */
 
 /* Resident-operand probe.  CTA b loads A_b and B_{c,b} (c < chains) once and
  * then accumulates C_{c,b} += A_b . B_{c,b}^T `iterations` times.
