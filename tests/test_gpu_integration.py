@@ -33,22 +33,26 @@ def stub(cuda):
 
 
 # (dtype, dot_input_precision, block_m, block_n, block_k): the reference's IEEE FP32
-# tiles (bench_tensor.py:499-503), its FP64 tiles (:497-498) and the one tile of its
-# NVIDIA set that the tcgen05 kernel takes (:504-511, M = 128).
+# tiles (bench_tensor.py:499-503), its FP64 tiles (:497-498) and its NVIDIA set for
+# the tcgen05 kinds (:504-511: 64x64, 64x128, 128x64 at K 32, or 64 for 8-bit).
 CASES = [(torch.float32, "ieee", 32, 32, 32), (torch.float32, "ieee", 32, 64, 32),
          (torch.float32, "ieee", 64, 32, 32), (torch.float32, "ieee", 64, 64, 32),
          (torch.float64, None, 32, 32, 16), (torch.float64, None, 32, 64, 16),
-         (torch.bfloat16, None, 128, 64, 32), (torch.float32, "tf32", 128, 64, 32)]
+         (torch.bfloat16, None, 64, 64, 32), (torch.bfloat16, None, 64, 128, 32),
+         (torch.bfloat16, None, 128, 64, 32), (torch.float16, None, 64, 128, 32),
+         (torch.float32, "tf32", 64, 64, 32), (torch.float32, "tf32", 128, 64, 32),
+         (torch.int8, None, 64, 128, 64), (torch.float8_e4m3fn, None, 64, 64, 64)]
 
 
 @pytest.mark.parametrize("dtype,precision,m,n,k", CASES)
 def test_stub_runs_reference_tiles_exactly(stub, cuda, dtype, precision, m, n, k):
     blocks, chains, iterations = 3, 2, 5
     gen = torch.Generator().manual_seed(m * n + k)
-    a = (torch.randint(-1, 2, (blocks, m, k), generator=gen).double() / 16).to(dtype)
-    b = (torch.randint(-1, 2, (chains, blocks, k, n), generator=gen).double() / 16).to(dtype)
-    out_dtype = torch.float64 if dtype == torch.float64 else torch.float32
-    c = torch.full((chains, blocks, m, n), float("nan"), dtype=out_dtype, device=cuda)
+    scale = 1 if dtype == torch.int8 else 16  # ternary, / 16 for the float kinds
+    a = (torch.randint(-1, 2, (blocks, m, k), generator=gen).double() / scale).to(dtype)
+    b = (torch.randint(-1, 2, (chains, blocks, k, n), generator=gen).double() / scale).to(dtype)
+    out_dtype = {torch.float64: torch.float64, torch.int8: torch.int32}.get(dtype, torch.float32)
+    c = torch.full((chains, blocks, m, n), -7, dtype=out_dtype, device=cuda)
     config = dict(block_m=m, block_n=n, block_k=k, num_warps=4, num_stages=1, chains=chains)
     stub["_launch_peak"](a.to(cuda), b.to(cuda), c, iterations, config,
                          dot_input_precision=precision)
@@ -58,13 +62,13 @@ def test_stub_runs_reference_tiles_exactly(stub, cuda, dtype, precision, m, n, k
 
 
 def test_stub_raises_reference_classifiable_rejection(stub, cuda):
-    """A 64-row tile of a tcgen05 kind (the reference's NVIDIA set) is rejected with
+    """A tile the library does not provide (32 rows on a tcgen05 kind) is rejected with
     the message the reference's _unsupported_reason accepts (tests/golden/tensor.json,
     status_classification), so the reference's sweep records it and goes on."""
-    a = torch.zeros((1, 64, 32), dtype=torch.bfloat16, device=cuda)
+    a = torch.zeros((1, 32, 32), dtype=torch.bfloat16, device=cuda)
     b = torch.zeros((2, 1, 32, 64), dtype=torch.bfloat16, device=cuda)
-    c = torch.zeros((2, 1, 64, 64), device=cuda)
-    config = dict(block_m=64, block_n=64, block_k=32, num_warps=4, num_stages=1, chains=2)
+    c = torch.zeros((2, 1, 32, 64), device=cuda)
+    config = dict(block_m=32, block_n=64, block_k=32, num_warps=4, num_stages=1, chains=2)
     with pytest.raises(RuntimeError, match="unsupported matrix format or tile"):
         stub["_launch_peak"](a, b, c, 1, config)
 

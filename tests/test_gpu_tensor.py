@@ -81,6 +81,10 @@ TC_CASES = [
     (INT8, 128, 256, 64, 2), (INT8, 256, 256, 128, 1),
     (FP8, 128, 128, 64, 2), (FP8, 256, 256, 128, 1),
     (MXF4, 128, 128, 128, 2), (MXF4, 256, 256, 256, 1), (MXF4, 128, 256, 512, 1),
+    # 64-row tiles (one M=64 accumulator, 16 rows per tensor-memory sub-partition),
+    # the reference's NVIDIA tile set (bench_tensor.py:504-511) among them.
+    (BF16, 64, 64, 32, 2), (BF16, 64, 128, 32, 2), (FP16, 64, 256, 64, 1),
+    (TF32, 64, 64, 32, 2), (INT8, 64, 128, 64, 2), (FP8, 64, 64, 64, 2),
 ]
 
 
@@ -203,12 +207,15 @@ def test_fp4_arithmetic_probe(cuda):
 
 
 def test_unsupported_tiles_are_capability_errors(cuda, native):
-    a = torch.zeros((1, 64, 64), dtype=torch.bfloat16, device=cuda)
+    """32-row tiles, and 64-row MX FP4 tiles (its scale layout follows M = 128)."""
+    a = torch.zeros((1, 64, 256), dtype=torch.uint8, device=cuda)
     c = torch.zeros((1, 1, 64, 64), device=cuda)
-    with pytest.raises(native.TcbError) as info:
-        native.tensor_peak(BF16, TCGEN05, a, a, c, blocks=1, blocks_per_sm=1, tile_m=64,
-                           tile_n=64, tile_k=64, chains=1, iterations=1)
-    assert info.value.is_capability
+    for dtype, m, k in ((BF16, 32, 64), (MXF4, 64, 256)):
+        with pytest.raises(native.TcbError) as info:
+            native.tensor_peak(dtype, TCGEN05, a, a, c, blocks=1, blocks_per_sm=1, tile_m=m,
+                               tile_n=64, tile_k=k, chains=1, iterations=1, scale_a=a,
+                               scale_b=a)
+        assert info.value.is_capability
 
 
 def test_kernel_info_reports_instruction(native, cuda):

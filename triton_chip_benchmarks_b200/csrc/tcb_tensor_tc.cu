@@ -10,7 +10,9 @@
 //      tcgen05.mma instructions (M=128, N=tile_n) that accumulate in tensor
 //      memory, committed to an mbarrier,
 //   5. reads the accumulators back with tcgen05.ld and stores C.
-// A 256-row tile is two M=128 accumulators.  When the accumulators plus the
+// A 256-row tile is two M=128 accumulators.  A 64-row tile (not MX FP4) is one
+// M=64 accumulator, which tensor memory holds 16 rows per 32-lane
+// sub-partition: row 16w + i in lane 32w + i, i < 16.  When the accumulators plus the
 // scale factors do not fit the CTA's tensor-memory share at once, the
 // (half, chain) accumulator groups run in consecutive passes; every group
 // still receives exactly `iterations` accumulations of its tile product.
@@ -40,6 +42,7 @@ struct TcArgs {
   int* status;
   int blocks, tile_m, tile_n, kbytes, panel, chains, iterations;
   int halves, ksteps, groups, groups_per_pass, tmem_cols, sf_groups;
+  int mma_m;        // rows of one accumulator: 128, or 64 for a 64-row tile
   uint32_t layout;  // descriptor swizzle code: 2 = 128B, 4 = 64B, 6 = 32B
   uint32_t idesc;   // instruction descriptor
 };
@@ -238,10 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = __syncthreads_and(done) != 0;
     if (!ok) break;
 
-    // 5. Epilogue: warp w reads rows 32w..32w+31 of each accumulator.
+    // 5. Epilogue: warp w reads lanes 32w..32w+31 of each accumulator, which
+    //    hold rows 32w..32w+31 (M=128) or, in lanes 32w..32w+15, rows
+    //    16w..16w+15 (M=64).  Every lane takes part in the warp-wide loads.
+    const bool m64 = args.mma_m == 64;
+    const bool live = !m64 || lane < 16;
     for (int g = g0; g < g1; ++g) {
       const int c = g / args.halves, h = g - c * args.halves;
-      const int row = h * 128 + 32 * warp + lane;
+      const int row = m64 ? 16 * warp + (lane & 15) : h * 128 + 32 * warp + lane;
       uint32_t* dst = static_cast<uint32_t*>(args.c) +
                       (static_cast<size_t>(c * args.blocks + blk) * M + row) * N;
       const uint32_t t_row = tbase + ((32u * warp) << 16) + static_cast<uint32_t>((g - g0) * N);
@@ -249,10 +256,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32cols(t_row + 32 * j, r);
         tmem_wait_ld();
-        uint4* out = reinterpret_cast<uint4*>(dst + 32 * j);
+        if (live) {
+          uint4* out = reinterpret_cast<uint4*>(dst + 32 * j);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          out[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          for (int q = 0; q < 8; ++q)
+            out[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+        }
       }
     }
     tc_fence_before();
@@ -360,11 +369,11 @@ int elem_bits(int kind) {
   return 0;
 }
 
-// Instruction descriptor (M = 128, K-major A and B, dense).
-uint32_t make_idesc(int kind, int n) {
+// Instruction descriptor (M = 128 or 64, K-major A and B, dense).
+uint32_t make_idesc(int kind, int n, int m) {
   uint32_t d = 0;
   d |= static_cast<uint32_t>(n >> 3) << 17;
-  d |= static_cast<uint32_t>(128 >> 4) << 24;
+  d |= static_cast<uint32_t>(m >> 4) << 24;
   if (kind == kMXF4) {
     d |= 1u << 7;   // A: E2M1
     d |= 1u << 10;  // B: E2M1
@@ -399,7 +408,7 @@ uint32_t make_idesc(int kind, int n) {
 struct Plan {
   int kind = -1;
   int kbytes = 0, panel = 0, halves = 0, ksteps = 0, groups = 0, groups_per_pass = 0;
-  int tmem_cols = 0, sf_cols = 0, smem_bytes = 0, smem_request = 0;
+  int tmem_cols = 0, sf_cols = 0, smem_bytes = 0, smem_request = 0, mma_m = 128;
   uint32_t layout = 0;
   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE;
 };
@@ -409,7 +418,10 @@ int make_plan(int dtype, int tile_m, int tile_n, int tile_k, int chains, int bps
   Plan p;
   p.kind = kind_for(dtype);
   if (p.kind < 0) return TCB_ERR_UNSUPPORTED;
-  if (tile_m != 128 && tile_m != 256) return TCB_ERR_UNSUPPORTED;
+  // 64-row tiles run one M=64 MMA; MX FP4 keeps M = 128 (its scale-factor
+  // layout in tensor memory follows M).
+  const bool m64 = tile_m == 64 && p.kind != kMXF4;
+  if (tile_m != 128 && tile_m != 256 && !m64) return TCB_ERR_UNSUPPORTED;
   if (tile_n < 32 || tile_n > 256 || tile_n % 32) return TCB_ERR_UNSUPPORTED;
   if (chains < 1 || chains > 2) return TCB_ERR_INVALID_ARGUMENT;
   if (bps != 1 && bps != 2 && bps != 4 && bps != 8 && bps != 16) return TCB_ERR_INVALID_ARGUMENT;
@@ -429,7 +441,8 @@ int make_plan(int dtype, int tile_m, int tile_n, int tile_k, int chains, int bps
   p.swizzle = p.panel == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
               : p.panel == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                               : CU_TENSOR_MAP_SWIZZLE_32B;
-  p.halves = tile_m / 128;
+  p.mma_m = m64 ? 64 : 128;
+  p.halves = m64 ? 1 : tile_m / 128;
   p.ksteps = p.kbytes / kMmaKBytes;
   p.groups = p.halves * chains;
   p.tmem_cols = 512 / bps;
@@ -520,7 +533,8 @@ int tc_tensor_peak(int dtype, const void* A, const void* B, const void* SA, cons
   args.tmem_cols = p.tmem_cols;
   args.sf_groups = p.ksteps * 2;
   args.layout = p.layout;
-  args.idesc = make_idesc(p.kind, tile_n);
+  args.mma_m = p.mma_m;
+  args.idesc = make_idesc(p.kind, tile_n, p.mma_m);
   KernelFn fn = kernel_for(p.kind, p.ksteps);
   if (fn == nullptr) return TCB_ERR_UNSUPPORTED;
   // Raise the dynamic shared-memory cap once per (kernel, device).
