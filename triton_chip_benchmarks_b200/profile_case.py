@@ -8,6 +8,7 @@ validates its first launch against the product's checks, then launches
 those launches (CUDA events).
 
   python -m triton_chip_benchmarks_b200.profile_case copy --mib 1024 --variant bulk
+  python -m triton_chip_benchmarks_b200.profile_case read --mib 1024 --block 4096
   python -m triton_chip_benchmarks_b200.profile_case tensor --dtype bf16 --tile 256x256x64
   python -m triton_chip_benchmarks_b200.profile_case vector --dtype fp32
   python -m triton_chip_benchmarks_b200.profile_case gemm --dtype fp4 --size 4096
@@ -51,6 +52,26 @@ def case_copy(args) -> dict:
     ms = _time(run, args.launches)
     return {"case": "copy", "variant": args.variant, "bytes": n, "ms_per_launch": ms,
             "gbps": 2 * n / (ms * 1e6)}
+
+
+def case_read(args) -> dict:
+    """fp32 read-and-sum (tcb_read), the suite's read pattern; sink checked against torch."""
+    n = (args.mib << 20) // 4
+    src = torch.randn(n, device="cuda")
+    blocks = -(-n // args.block)
+    sink = torch.empty(blocks, device="cuda")
+
+    def run():
+        _native.read(src, _native.READ_FP32, n, sink, args.block, args.threads)
+
+    run()
+    torch.cuda.synchronize()
+    expected = torch.nn.functional.pad(src.double(), (0, blocks * args.block - n))
+    expected = expected.view(blocks, args.block).sum(1)
+    assert torch.allclose(sink.double(), expected, rtol=1e-4, atol=1e-2), "read mismatch"
+    ms = _time(run, args.launches)
+    return {"case": "read", "bytes": 4 * n, "block": args.block, "threads": args.threads,
+            "ms_per_launch": ms, "gbps": (4 * n + 4 * blocks) / (ms * 1e6)}
 
 
 def case_tensor(args) -> dict:
@@ -137,6 +158,11 @@ def main(argv=None):
     p.add_argument("--threads", type=int, default=0)
     p.add_argument("--blocks", type=int, default=0)
     p.add_argument("--launches", type=int, default=3)
+    p = sub.add_parser("read")
+    p.add_argument("--mib", type=int, default=1024)
+    p.add_argument("--block", type=int, default=4096, help="elements summed per CTA")
+    p.add_argument("--threads", type=int, default=256)
+    p.add_argument("--launches", type=int, default=3)
     p = sub.add_parser("tensor")
     p.add_argument("--dtype", default="bf16", choices=sorted(NATIVE))
     p.add_argument("--kernel", default="tcgen05", choices=("tcgen05", "dmma", "simt", "simt_reg"))
@@ -160,8 +186,8 @@ def main(argv=None):
     p.add_argument("--launches", type=int, default=3)
     args = parser.parse_args(argv)
     torch.cuda.set_device(0)
-    result = {"copy": case_copy, "tensor": case_tensor, "vector": case_vector,
-              "gemm": case_gemm}[args.case](args)
+    result = {"copy": case_copy, "read": case_read, "tensor": case_tensor,
+              "vector": case_vector, "gemm": case_gemm}[args.case](args)
     print(json.dumps(result))
 
 
