@@ -40,6 +40,7 @@ typedef struct CUstream_st *tcb_stream_t; /* identical to cudaStream_t */
 #define TCB_ERR_DEVICE (-5)           /* a device query failed */
 #define TCB_ERR_TIMEOUT (-6)          /* device-side bounded wait ran out (status word only) */
 #define TCB_ERR_ALIGNMENT (-7)        /* pointer or size not aligned as the kernel requires */
+#define TCB_ERR_SCRATCH_LIMIT (-8)    /* problem too large for the library's fixed scratch array */
 
 /* Human-readable text for a status code (static storage). */
 const char *tcb_strerror(int status);
@@ -191,6 +192,27 @@ long long tcb_mx_scales_packed_bytes(int rows, int groups);
  * bytes, 16-byte aligned.  Run once per scale tensor (data preparation, not
  * part of the GEMM).  No counterpart in the reference. */
 int tcb_mx_scales_pack(const void *src, void *dst, int rows, int groups, tcb_stream_t stream);
+
+/* MX FP4 GEMM that allocates nothing, for callers that cannot allocate device
+ * memory (a plugin whose host framework owns all device memory through its
+ * own pool, or a path where cudaMalloc/cudaFree and their synchronisation are
+ * not allowed).  No counterpart in the reference.
+ * Same contract as tcb_gemm(TCB_T_MXF4, ...) except that SA [M][K/32] and
+ * SB [N][K/32] are plain row-major E8M0 scales (any alignment): the call packs
+ * them into a fixed 8 MiB scratch array in the library's device image, then
+ * runs the GEMM, all in order on `stream`.  Limits: K % 32 == 0
+ * (TCB_ERR_UNSUPPORTED otherwise), and the packed scales of A and of B, each
+ * rounded up to 256 bytes, must fit in 8 MiB (M = N = 16384 at K = 8192 does),
+ * otherwise TCB_ERR_SCRATCH_LIMIT before anything is launched.
+ * The scratch array is held by every device that loads the library until the
+ * process exits.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture.  Every call shares the one array and
+ * rewrites all of the part it reads: calls whose work overlaps on the GPU
+ * (different streams, or other host threads) race on it and must be
+ * serialised by the caller. */
+int tcb_gemm_mxf4_noalloc(const void *A, const void *B, const void *SA, const void *SB, void *C,
+                          int M, int N, int K, int blocks, int *status_dev, tcb_stream_t stream);
 
 /* ------------------------------------------------------- kernel info */
 #define TCB_FAMILY_COPY 0

@@ -24,6 +24,7 @@ ERR_LAUNCH = -4
 ERR_DEVICE = -5
 ERR_TIMEOUT = -6
 ERR_ALIGNMENT = -7
+ERR_SCRATCH_LIMIT = -8
 
 COPY_LDG128, COPY_BULK = 0, 1
 READ_FP32, READ_FP16, READ_BF16 = 0, 1, 2
@@ -39,7 +40,7 @@ FAMILY_COPY, FAMILY_READ, FAMILY_VECTOR, FAMILY_TENSOR, FAMILY_GEMM = 0, 1, 2, 3
 EXPORTED_SYMBOLS = (
     "tcb_strerror", "tcb_version", "tcb_device_query", "tcb_copy", "tcb_read",
     "tcb_vector_chains", "tcb_vector_chains_imm", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_packed_bytes",
-    "tcb_mx_scales_pack", "tcb_kernel_info",
+    "tcb_mx_scales_pack", "tcb_kernel_info", "tcb_gemm_mxf4_noalloc",
 )
 
 
@@ -132,6 +133,7 @@ def load() -> ctypes.CDLL:
         lib.tcb_tensor_peak.argtypes = [i, i, vp, vp, vp, vp, vp, i, i, i, i, i, i, i, vp, vp]
         lib.tcb_gemm.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_mx_scales_pack.argtypes = [vp, vp, i, i, vp]
+        lib.tcb_gemm_mxf4_noalloc.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_mx_scales_packed_bytes.argtypes = [i, i]
         lib.tcb_kernel_info.argtypes = [i, i, i, i, i, i, i, i, ctypes.POINTER(KernelInfo)]
         for name in EXPORTED_SYMBOLS:

@@ -62,6 +62,8 @@ extern "C" const char* tcb_strerror(int status) {
       return "device-side bounded wait timed out";
     case TCB_ERR_ALIGNMENT:
       return "pointer or size is not aligned as the kernel requires";
+    case TCB_ERR_SCRATCH_LIMIT:
+      return "problem exceeds the library's fixed scratch array (8 MiB of packed MX scales)";
     default:
       return "unknown status";
   }
