@@ -79,10 +79,12 @@ int tcb_device_query(int device, tcb_device_props *out);
  * `threads` is the CTA size (0: 512).  For BULK the CTA is one warp and
  * `threads` is the depth of the shared-memory ring in 32 KiB chunks (2..8,
  * 0: 2; the default grid is 2 CTAs per SM). src and dst must not overlap.
+ * A bulk-copy ring wait that runs out writes TCB_ERR_TIMEOUT into
+ * `status_dev` (may be NULL; the LDG128 and byte kernels never wait).
  * Replaces launch_copy (bench_bandwidth.py:43-47) and copy_kernel
  * (bench_bandwidth.py:36-40). */
 int tcb_copy(const void *src, void *dst, size_t bytes, int variant, int blocks, int threads,
-             tcb_stream_t stream);
+             int *status_dev, tcb_stream_t stream);
 
 #define TCB_READ_FP32 0
 #define TCB_READ_FP16 1
@@ -214,6 +216,15 @@ int tcb_mx_scales_pack(const void *src, void *dst, int rows, int groups, tcb_str
 int tcb_gemm_mxf4_noalloc(const void *A, const void *B, const void *SA, const void *SB, void *C,
                           int M, int N, int K, int blocks, int *status_dev, tcb_stream_t stream);
 
+/* --------------------------------------------------------- self-test */
+/* Runs the library's bounded device-side wait against an mbarrier whose phase
+ * can never complete (armed for bytes no copy delivers), with a limit of
+ * `limit_ns` (0..1e9).  The kernel must give up, write TCB_ERR_TIMEOUT into
+ * `status_dev` (required) and return, leaving the context usable: this is the
+ * path every probe kernel takes when one of its waits runs out.  No
+ * counterpart in the reference (its Triton kernels have no device waits). */
+int tcb_selftest_bounded_wait(long long limit_ns, int *status_dev, tcb_stream_t stream);
+
 /* ------------------------------------------------------- kernel info */
 #define TCB_FAMILY_COPY 0
 #define TCB_FAMILY_READ 1
@@ -231,6 +242,9 @@ typedef struct tcb_kernel_info_t {
   int tensor_core;           /* 1: the arithmetic runs on tensor cores */
   char instruction[128];     /* the arithmetic instruction written in the kernel source */
   char execution_kind[16];   /* "tensor" or "simt" */
+  int pipeline_stages;       /* GEMM: shared-memory operand stages of the ring (else 0) */
+  int tile_m, tile_n;        /* GEMM: output tile of one CTA or CTA cluster (else 0) */
+  int cluster_ctas;          /* GEMM: CTAs that share one output tile (1, or 2 for pairs) */
 } tcb_kernel_info_t;
 
 /* Static facts about the kernel a launch with these arguments would run.
@@ -239,7 +253,8 @@ typedef struct tcb_kernel_info_t {
  *   READ   : dtype, threads
  *   VECTOR : dtype, threads, elems_per_thread, unroll
  *   TENSOR : dtype, variant, tile_m, tile_n, tile_k, chains (blocks_per_sm via a6)
- *   GEMM_FP4 (any GEMM dtype): dtype
+ *   GEMM_FP4 (any GEMM dtype): dtype, M, N (M, N = 0: a large problem); the
+ *            kernel tcb_gemm would run for that shape on the current device
  * Replaces the CompiledKernel metadata read by _compiled_info
  * (bench_tensor.py:984-1146) and inspect_assembly (bench_vector.py:623-799). */
 int tcb_kernel_info(int family, int a0, int a1, int a2, int a3, int a4, int a5, int a6,

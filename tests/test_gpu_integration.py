@@ -1,4 +1,4 @@
-"""The ctypes stub of INTEGRATION.md, executed against the built library (GPU).
+"""The reference-side ctypes stub (tcb_binding.py) against the built library (GPU).
 
 The stub is what a maintainer adds beside the reference's scripts.  Here its
 _launch_peak runs tile shapes from the reference's own sweep
@@ -8,28 +8,17 @@ reference's _peak_inputs lays them out (bench_tensor.py:647-672: A
 result must equal iterations x (A . B) exactly.
 """
 
-import re
-from pathlib import Path
-
 import numpy as np
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-REPO = Path(__file__).resolve().parents[1]
-LIBRARY = REPO / "triton_chip_benchmarks_b200" / "libtcb.so"
-PLACEHOLDER = "/path/to/triton_chip_benchmarks_b200/libtcb.so"
-
 
 @pytest.fixture(scope="module")
 def stub(cuda):
-    text = (REPO / "INTEGRATION.md").read_text()
-    block = re.findall(r"```python\n(.*?)```", text, flags=re.S)[0]
-    assert PLACEHOLDER in block
-    namespace = {}
-    exec(compile(block.replace(PLACEHOLDER, str(LIBRARY)), "INTEGRATION.md", "exec"), namespace)
-    return namespace
+    from triton_chip_benchmarks_b200 import tcb_binding
+    return vars(tcb_binding)
 
 
 # (dtype, dot_input_precision, block_m, block_n, block_k): the reference's IEEE FP32

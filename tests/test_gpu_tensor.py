@@ -296,6 +296,38 @@ def test_gemm_cuda_core_kernel_info(native, cuda):
     assert fp32["local_bytes_per_thread"] == 0 and fp64["local_bytes_per_thread"] == 0
 
 
+@pytest.mark.parametrize("dtype,m,n,k", [(INT8, 3400, 3328, 256), (BF16, 3328, 3400, 192),
+                                         (FP8, 3584, 3352, 128)])
+def test_gemm_256_row_tiles(cuda, native, dtype, m, n, k):
+    """Problems with at least as many 256 x 256 tiles as SMs run on the two-accumulator
+    kernel (256-row tiles); M tails that are not multiples of 256 are masked."""
+    info = native.kernel_info(native.FAMILY_GEMM, dtype, m, n)
+    assert (info["tile_m"], info["tile_n"], info["cluster_ctas"]) == (256, 256, 1)
+    assert info["pipeline_stages"] >= 2
+    a, b = _operands(dtype, 1, 1, m, n, k, seed=m + k)
+    a, b = a[0], b[0, 0]
+    out_dtype = torch.int32 if dtype == INT8 else torch.float32
+    c = torch.full((m, n), -7, dtype=out_dtype, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    native.gemm(dtype, a.to(cuda), b.to(cuda), c, m, n, k, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = oracle_tensor.resident_reference(_host(a), _host(b), 1, NAME[dtype])
+    assert np.array_equal(c.cpu().numpy().astype(np.float64), ref.astype(np.float64))
+
+
+def test_gemm_kernel_info_follows_the_shape(cuda, native):
+    """Small problems use 128-row tiles; MX FP4 above 128 rows uses CTA pairs."""
+    small = native.kernel_info(native.FAMILY_GEMM, BF16, 1024, 1024)
+    assert (small["tile_m"], small["cluster_ctas"]) == (128, 1)
+    pair = native.kernel_info(native.FAMILY_GEMM, MXF4, 8192, 8192)
+    assert (pair["tile_m"], pair["tile_n"], pair["cluster_ctas"]) == (256, 256, 2)
+    assert "cta_group::2" in pair["instruction"]
+    single = native.kernel_info(native.FAMILY_GEMM, MXF4, 128, 8192)
+    assert (single["tile_m"], single["cluster_ctas"]) == (128, 1)
+    assert "cta_group::1" in single["instruction"]
+
+
 def test_gemm_persistent_tiles(cuda, native):
     """More tiles than CTAs: each CTA walks several tiles through one accumulator."""
     m, n, k = 1024, 1024, 512

@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "tcb_strerror", "tcb_version", "tcb_device_query", "tcb_copy", "tcb_read",
     "tcb_vector_chains", "tcb_vector_chains_imm", "tcb_tensor_peak", "tcb_gemm", "tcb_mx_scales_packed_bytes",
     "tcb_mx_scales_pack", "tcb_kernel_info", "tcb_gemm_mxf4_noalloc",
+    "tcb_selftest_bounded_wait",
 )
 
 
@@ -95,6 +96,9 @@ class KernelInfo(ctypes.Structure):
         ("tensor_core", ctypes.c_int),
         ("instruction", ctypes.c_char * 128),
         ("execution_kind", ctypes.c_char * 16),
+        ("pipeline_stages", ctypes.c_int),
+        ("tile_m", ctypes.c_int), ("tile_n", ctypes.c_int),
+        ("cluster_ctas", ctypes.c_int),
     ]
 
 
@@ -126,7 +130,7 @@ def load() -> ctypes.CDLL:
         lib.tcb_strerror.argtypes, lib.tcb_strerror.restype = [i], ctypes.c_char_p
         lib.tcb_version.argtypes, lib.tcb_version.restype = [], ctypes.c_char_p
         lib.tcb_device_query.argtypes = [i, ctypes.POINTER(DeviceProps)]
-        lib.tcb_copy.argtypes = [vp, vp, sz, i, i, i, vp]
+        lib.tcb_copy.argtypes = [vp, vp, sz, i, i, i, vp, vp]
         lib.tcb_read.argtypes = [vp, i, ll, vp, i, i, vp]
         lib.tcb_vector_chains.argtypes = [i, vp, vp, vp, ll, i, i, i, i, i, vp]
         lib.tcb_vector_chains_imm.argtypes = [i, vp, vp, vp, ll, i, i, i, i, i, vp]
@@ -135,6 +139,7 @@ def load() -> ctypes.CDLL:
         lib.tcb_mx_scales_pack.argtypes = [vp, vp, i, i, vp]
         lib.tcb_gemm_mxf4_noalloc.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
         lib.tcb_mx_scales_packed_bytes.argtypes = [i, i]
+        lib.tcb_selftest_bounded_wait.argtypes = [ll, vp, vp]
         lib.tcb_kernel_info.argtypes = [i, i, i, i, i, i, i, i, ctypes.POINTER(KernelInfo)]
         for name in EXPORTED_SYMBOLS:
             if name not in ("tcb_strerror", "tcb_version"):
@@ -206,8 +211,10 @@ def device_query(device: int) -> Device:
 
 
 def copy(src, dst, nbytes: int, variant: int = COPY_LDG128, blocks: int = 0, threads: int = 0,
-         stream=None) -> None:
-    check(load().tcb_copy(_ptr(src), _ptr(dst), nbytes, variant, blocks, threads,
+         stream=None, *, status=None) -> None:
+    """dst[:nbytes] = src[:nbytes]; `status` (int32 device word) receives a
+    bulk-ring timeout, if any."""
+    check(load().tcb_copy(_ptr(src), _ptr(dst), nbytes, variant, blocks, threads, _ptr(status),
                           _stream(stream)), "tcb_copy")
 
 
@@ -260,6 +267,13 @@ def mx_scales_pack(src, dst, rows: int, groups: int, stream=None) -> None:
           "tcb_mx_scales_pack")
 
 
+def selftest_bounded_wait(limit_ns: int, status, stream=None) -> None:
+    """Launch the wait self-test: a bounded wait that cannot succeed, which must
+    write ERR_TIMEOUT into `status` and return."""
+    check(load().tcb_selftest_bounded_wait(limit_ns, _ptr(status), _stream(stream)),
+          "tcb_selftest_bounded_wait")
+
+
 def kernel_info(family: int, *args: int) -> dict:
     values = list(args) + [0] * (7 - len(args))
     info = KernelInfo()
@@ -274,4 +288,6 @@ def kernel_info(family: int, *args: int) -> dict:
         "tensor_core": bool(info.tensor_core),
         "instruction": info.instruction.decode(),
         "execution_kind": info.execution_kind.decode(),
+        "pipeline_stages": info.pipeline_stages,
+        "tile_m": info.tile_m, "tile_n": info.tile_n, "cluster_ctas": info.cluster_ctas,
     }

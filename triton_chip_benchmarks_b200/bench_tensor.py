@@ -715,13 +715,11 @@ def run_gemm(args, metadata) -> None:
         if key in GEMM_CONFIG:
             config = dict(GEMM_CONFIG[key])
         else:
-            sms = metadata.get("sm_count") or 148
-            tiles256 = -(-m // 256) * -(-n // 256)
-            pair = key == "fp4" and m > 128
-            halves = 2 if (pair or (key != "fp4" and m > 128 and tiles256 >= sms)) else 1
-            config = {"block_m": 128 * halves, "block_n": 256, "block_k_bytes": 128,
-                      "stages": 5 if pair else 3 if halves == 2 else 4, "persistent": True,
-                      "cta_pair": pair}
+            # The tile and ring the library runs for this shape, as it reports them.
+            shape = _native.kernel_info(_native.FAMILY_GEMM, NATIVE[key], m, n)
+            config = {"block_m": shape["tile_m"], "block_n": shape["tile_n"],
+                      "block_k_bytes": 128, "stages": shape["pipeline_stages"],
+                      "persistent": True, "cta_pair": shape["cluster_ctas"] == 2}
         row = {**base,
                "measurement_kind": (f"{descriptor['math_mode']}_gemm"
                                     if args.dtype in ("fp32", "fp64") else "dense_tensor_gemm"),

@@ -242,7 +242,7 @@ int copy_bulk_smem_bytes(int stages) { return stages * kBulkChunk; }
 using namespace tcb;
 
 extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, int blocks,
-                        int threads, tcb_stream_t stream) {
+                        int threads, int* status_dev, tcb_stream_t stream) {
   if (bytes == 0) return TCB_OK;
   if (src == nullptr || dst == nullptr) return TCB_ERR_INVALID_ARGUMENT;
   if (variant != TCB_COPY_LDG128 && variant != TCB_COPY_BULK) return TCB_ERR_INVALID_ARGUMENT;
@@ -279,7 +279,7 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
   if (blocks == 0) blocks = facts.sm_count * 2;
   copy_bulk_kernel<<<blocks, 32, smem, s>>>(static_cast<const unsigned char*>(src),
                                             static_cast<unsigned char*>(dst), bytes, stages,
-                                            nullptr);
+                                            status_dev);
   return launch_status();
 }
 

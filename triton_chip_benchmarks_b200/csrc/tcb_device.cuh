@@ -64,12 +64,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded phase wait.  Returns false (and leaves the barrier untouched) when
-// the phase did not complete within the timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// the phase did not complete within `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - start > kWaitTimeoutNs) return false;
+    if (globaltimer_ns() - start > limit_ns) return false;
   }
   return true;
 }
@@ -215,6 +216,10 @@ __device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr)
   uint32_t v;
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
 // Arrive on an mbarrier given by its cluster address, which may belong to the

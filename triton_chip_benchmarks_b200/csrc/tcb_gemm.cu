@@ -326,6 +326,11 @@ GemmFn gemm_fn(int kind, int halves) {
   return nullptr;
 }
 
+int gemm_stages(int kind, int halves) {
+  if (kind == gMXF4) return Tile<1, true>::kStages;
+  return halves == 2 ? Tile<2>::kStages : Tile<1>::kStages;
+}
+
 int gemm_smem(int kind, int halves) {
   if (kind == gMXF4) return Tile<1, true>::kSmem;
   return halves == 2 ? Tile<2>::kSmem : Tile<1>::kSmem;
@@ -427,19 +432,24 @@ const char* gemm_instruction(int kind) {
 
 }  // namespace
 
-int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
+int gemm_kernel_info(int dtype, int m, int n, tcb_kernel_info_t* out) {
   if (dtype == TCB_T_FP32 || dtype == TCB_T_FP64) return gemm_cuda_core_info(dtype, out);
   const int kind = gemm_kind(dtype);
   if (kind < 0) return TCB_ERR_UNSUPPORTED;
-  if (kind == gMXF4) {
-    const int rc = gemm_pair_info(out);
-    if (rc != TCB_OK) return rc;
+  if (m <= 0) m = 1 << 16;
+  if (n <= 0) n = 1 << 16;
+  DeviceFacts facts;
+  const int rc = current_device_facts(&facts);
+  if (rc != TCB_OK) return rc;
+  if (kind == gMXF4 && m > 128) {
+    const int prc = gemm_pair_info(out);
+    if (prc != TCB_OK) return prc;
     copy_str(out->instruction, sizeof(out->instruction),
              "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 (e2m1 x e2m1, ue8m0 -> f32)");
     copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
     return TCB_OK;
   }
-  const int halves = gemm_halves(kind, 1 << 16, 1 << 16, 1);
+  const int halves = gemm_halves(kind, m, n, facts.sm_count);
   cudaFuncAttributes attr;
   if (cudaFuncGetAttributes(&attr, reinterpret_cast<const void*>(gemm_fn(kind, halves))) !=
       cudaSuccess)
@@ -448,6 +458,10 @@ int gemm_kernel_info(int dtype, tcb_kernel_info_t* out) {
   out->dynamic_smem_bytes = gemm_smem(kind, halves);
   out->threads_per_block = (6 + kScaleWarps) * 32;
   out->tensor_core = 1;
+  out->pipeline_stages = gemm_stages(kind, halves);
+  out->tile_m = 128 * halves;
+  out->tile_n = kTileN;
+  out->cluster_ctas = 1;
   copy_str(out->instruction, sizeof(out->instruction), gemm_instruction(kind));
   copy_str(out->execution_kind, sizeof(out->execution_kind), "tensor");
   return TCB_OK;

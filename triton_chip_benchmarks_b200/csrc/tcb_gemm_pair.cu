@@ -27,8 +27,8 @@
 //               swizzled shared staging and TMA tensor stores;
 //   warps 6-9   scale writers: move this CTA's staged scales into its scale
 //               slot and arrive on the leader's full[s].
-// Every wait is bounded; a timeout raises this CTA's abort flag (the peer's
-// waits then time out too).  A cluster barrier follows barrier set-up and
+// Every wait is bounded; a wait that fails raises the abort flag of both
+// CTAs, so the pair leaves its loops together.  A cluster barrier follows barrier set-up and
 // precedes teardown, so neither CTA exits while its peer may still signal its
 // barriers or read its shared memory.
 //
@@ -116,10 +116,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   cluster_sync_all();  // both CTAs' barriers initialised and tensor memory allocated
   tc_fence_after();
   const uint32_t tbase = tmem_slot;
+  // An abort on either CTA stops both: a wait that fails also raises the
+  // peer's flag (a store into its shared memory, which stays valid until the
+  // teardown cluster barrier), so neither CTA sits out a full timeout on
+  // barriers the other no longer signals.
+  const uint32_t peer_abort = mapa_shared(smem_addr(const_cast<int*>(&abort_flag)), rank ^ 1u);
+  auto pair_wait = [&](uint64_t* bar, uint32_t parity) {
+    if (wait_or_abort(bar, parity, &abort_flag, args.status)) return true;
+    st_shared_cluster_u32(peer_abort, 1u);
+    return false;
+  };
   if (threadIdx.x == 0 && rank != 0) {
     // The pair MMA addresses both CTAs' tensor memory with the leader's column base.
     if (ld_shared_cluster_u32(mapa_shared(smem_addr(&tmem_slot), 0)) != tbase) {
       abort_flag = 1;
+      st_shared_cluster_u32(peer_abort, 1u);
       report_status(args.status, TCB_ERR_DEVICE);
     }
   }
@@ -138,7 +149,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
           const int s = it % kPairStages;
           const uint32_t phase = static_cast<uint32_t>(it / kPairStages) & 1u;
-          if (!wait_or_abort(&empty[s], phase ^ 1u, &abort_flag, args.status)) break;
+          if (!pair_wait(&empty[s], phase ^ 1u)) break;
           uint8_t* stage = smem + s * kPairStageBytes;
           const uint32_t lead_loaded = mapa_shared(smem_addr(&loaded[s]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&loaded[s], 2 * (kPairStageA + kPairStageB));
@@ -161,15 +172,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint32_t smem0 = smem_addr(smem) >> 4;
       int it = 0, ti = 0;
       for (int t = pair; t < tiles && !abort_flag; t += pairs, ++ti) {
-        if (!wait_or_abort(&acc_empty, (static_cast<uint32_t>(ti) & 1u) ^ 1u, &abort_flag,
-                                   args.status))
-          break;
+        if (!pair_wait(&acc_empty, (static_cast<uint32_t>(ti) & 1u) ^ 1u)) break;
         tc_fence_after();
         for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
           const int s = it % kPairStages;
           const uint32_t phase = static_cast<uint32_t>(it / kPairStages) & 1u;
-          if (!wait_or_abort(&loaded[s], phase, &abort_flag, args.status)) break;
-          if (!wait_or_abort(&full[s], phase, &abort_flag, args.status)) break;
+          if (!pair_wait(&loaded[s], phase)) break;
+          if (!pair_wait(&full[s], phase)) break;
           tc_fence_after();
           const uint32_t a_lo = smem0 + static_cast<uint32_t>(s * kPairStageBytes >> 4);
           const uint32_t b_lo = a_lo + (kPairStageA >> 4);
@@ -198,8 +207,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint8_t* epi_stage = smem + kPairStages * kPairStageBytes + (warp - 2) * kEpiWarpBytes;
     int ti = 0, issued = 0;
     for (int t = pair; t < tiles; t += pairs, ++ti) {
-      if (!wait_or_abort(&acc_full, static_cast<uint32_t>(ti) & 1u, &abort_flag, args.status))
-        break;
+      if (!pair_wait(&acc_full, static_cast<uint32_t>(ti) & 1u)) break;
       tc_fence_after();
       int tm, tn;
       tile_coords(t, args.tiles_m, args.tiles_n, &tm, &tn);
@@ -238,7 +246,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
         const int s = it % kPairStages;
         const uint32_t phase = static_cast<uint32_t>(it / kPairStages) & 1u;
-        if (!wait_or_abort(&sloaded[s], phase, &abort_flag, args.status)) break;
+        if (!pair_wait(&sloaded[s], phase)) break;
         const uint8_t* ss = smem + s * kPairStageBytes + kPairStageA + kPairStageB + lane * 8;
         uint2 fa[4], fb[kTileN / 32];
 #pragma unroll
@@ -314,6 +322,10 @@ int gemm_pair_info(tcb_kernel_info_t* out) {
   out->dynamic_smem_bytes = kPairSmem;
   out->threads_per_block = kPairThreads;
   out->tensor_core = 1;
+  out->pipeline_stages = kPairStages;
+  out->tile_m = 2 * kPairRows;
+  out->tile_n = kTileN;
+  out->cluster_ctas = 2;
   return TCB_OK;
 }
 

@@ -20,7 +20,7 @@ int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out);
 int read_kernel_info(int dtype, int threads, tcb_kernel_info_t* out);
 int vector_kernel_info(int dtype, int threads, int elems_per_thread, int unroll,
                        tcb_kernel_info_t* out);
-int gemm_kernel_info(int dtype, tcb_kernel_info_t* out);
+int gemm_kernel_info(int dtype, int m, int n, tcb_kernel_info_t* out);
 int gemm_cuda_core_info(int dtype, tcb_kernel_info_t* out);
 int gemm_cuda_core(int dtype, const void* A, const void* B, void* C, int M, int N, int K,
                    cudaStream_t stream);

@@ -1,0 +1,136 @@
+"""ctypes binding of libtcb.so for the reference suite's own scripts.
+
+This is the module a maintainer of the reference suite
+(huangyiqun/triton_chip_benchmarks) places beside its scripts as
+``tcb_binding.py`` and imports from ``bench_bandwidth.py``, ``bench_vector.py``
+and ``bench_tensor.py`` in place of their Triton launch wrappers::
+
+    from tcb_binding import launch_copy, launch_read, launch_vector, _launch_peak, _launch
+
+Each function keeps the signature of the wrapper it replaces (file:line beside
+it) and calls one entry point of the C ABI (include/tcb.h).  It imports only
+ctypes, weakref and torch; the library path comes from ``TCB_LIBRARY`` or
+defaults to the ``libtcb.so`` built beside this file.
+"""
+
+import ctypes
+import os
+import weakref
+
+import torch
+
+_lib = ctypes.CDLL(os.environ.get("TCB_LIBRARY") or
+                   os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtcb.so"))
+_vp, _i, _ll, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t
+_lib.tcb_copy.argtypes = [_vp, _vp, _sz, _i, _i, _i, _vp, _vp]
+_lib.tcb_read.argtypes = [_vp, _i, _ll, _vp, _i, _i, _vp]
+_lib.tcb_vector_chains.argtypes = [_i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]
+_lib.tcb_vector_chains_imm.argtypes = [_i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]
+_lib.tcb_tensor_peak.argtypes = [_i, _i, _vp, _vp, _vp, _vp, _vp] + [_i] * 7 + [_vp, _vp]
+_lib.tcb_gemm.argtypes = [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]
+_lib.tcb_strerror.restype = ctypes.c_char_p
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+# make(t) for a tensor t, computed at t's first use (the reference's first launch,
+# before validation and timing) and again only if t is modified in place.  Keyed by
+# the tensor object, not its address: the caching allocator hands a freed address to
+# the next tensor, and an address-keyed entry would then be stale.
+_derived = {}
+
+def _once(t, make):
+    entry = _derived.get(id(t))
+    if entry is None or entry[0]() is not t or entry[1] != t._version:
+        ref = weakref.ref(t, lambda _, key=id(t): _derived.pop(key, None))
+        entry = _derived[id(t)] = (ref, t._version, make(t))
+    return entry[2]
+
+# The reference's peak sweep skips a configuration on triton.OutOfResources and records
+# one as unsupported when _unsupported_reason accepts the RuntimeError's message
+# (bench_tensor.py:94-142, 1205-1220); TCB_ERR_UNSUPPORTED's message is worded for it.
+
+def _check(rc):
+    if rc == -3:                                            # TCB_ERR_RESOURCE
+        import triton
+        raise triton.OutOfResources(0, 0, _lib.tcb_strerror(rc).decode())
+    if rc != 0:
+        raise RuntimeError(_lib.tcb_strerror(rc).decode())
+
+# bench_bandwidth.launch_copy(src, dst, block_size, num_warps), bench_bandwidth.py:43-47
+
+def launch_copy(src, dst, block_size, num_warps):
+    _check(_lib.tcb_copy(src.data_ptr(), dst.data_ptr(), src.numel() * src.element_size(),
+                         1, 0, 0, None, _stream()))  # bulk-copy kernel, tuned grid
+
+# bench_bandwidth.launch_read(src, sink, block_size, num_warps, vendor_name),
+# bench_bandwidth.py:62-67
+
+def launch_read(src, sink, block_size, num_warps, vendor_name):
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[src.dtype]
+    _check(_lib.tcb_read(src.data_ptr(), code, src.numel(), sink.data_ptr(), block_size,
+                         (num_warps or 4) * 32, _stream()))
+
+# bench_vector.launch_vector(...), bench_vector.py:1032-1051: grid=(blocks,), BLOCK_SIZE
+# elements per program.
+# The reference passes every argument positionally (bench_vector.py:1411-1416); the
+# options after use_dp4a are off on NVIDIA.  The coefficients go to the kernel by
+# value (tcb_vector_chains_imm), from a host copy made once per coefficient tensor.
+# The 16-bit kernels work on packed pairs, so a block of one element per thread runs
+# as half the threads with two elements each (the same elements and iterations).
+
+def launch_vector(kernel, grid, inputs, output, coefficients, elements, iterations,
+                  block_size, unroll, use_explicit_fma, num_warps, is_int8=False,
+                  use_dp4a=False, *_, **__):
+    dtype = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2, torch.float64: 3}.get(
+        inputs.dtype, 4 if use_dp4a else 6)
+    threads = (num_warps or 4) * 32
+    if dtype in (0, 1) and block_size < 2 * threads:
+        threads = block_size // 2
+    host = _once(coefficients, lambda t: t.cpu().contiguous())
+    _check(_lib.tcb_vector_chains_imm(dtype, inputs.data_ptr(), output.data_ptr(),
+                                      host.data_ptr(), elements, iterations, grid[0],
+                                      threads, block_size // threads, unroll, _stream()))
+
+# bench_tensor._launch_peak(a, b, c, iterations, config, dot_input_precision, scales),
+# bench_tensor.py:581-600.
+# IEEE fp32 runs on the register-resident SIMT kernel (variant 3), which takes the
+# reference's 32- and 64-wide tiles; fp64 runs on DMMA (variant 1) where DMMA takes the
+# tile, else on the same SIMT kernel; the rest on tcgen05 (variant 0).  The choice is
+# made at the first launch of a shape (a rejected shape launches nothing).
+_variant = {}
+
+def _launch_peak(a, b, c, iterations, config, dot_input_precision=None, scales=None):
+    code = {torch.bfloat16: 0, torch.float16: 1, torch.float64: 4, torch.int8: 5,
+            torch.float8_e4m3fn: 6, torch.uint8: 7}.get(a.dtype)
+    if a.dtype == torch.float32:
+        code = 2 if dot_input_precision == "tf32" else 3
+    b_nk = _once(b, lambda t: t.transpose(-1, -2).contiguous())  # the ABI takes K-contiguous B
+    sa, sb = scales if scales is not None else (None, None)
+    shape = (code, config["block_m"], config["block_n"], config["block_k"], b.shape[0])
+    for variant in [_variant[shape]] if shape in _variant else {3: [3], 4: [1, 3]}.get(code, [0]):
+        rc = _lib.tcb_tensor_peak(code, variant, a.data_ptr(), b_nk.data_ptr(),
+                                  sa.data_ptr() if sa is not None else None,
+                                  sb.data_ptr() if sb is not None else None, c.data_ptr(),
+                                  a.shape[0], 1, config["block_m"], config["block_n"],
+                                  config["block_k"], b.shape[0], iterations, None, _stream())
+        if rc != -2:                                         # TCB_ERR_UNSUPPORTED: next variant
+            _variant[shape] = variant
+            break
+    _check(rc)
+
+# bench_tensor._launch(a, b, c, config, dot_input_precision) of --mode gemm,
+# bench_tensor.py:235-246:
+# a [M, K], b [K, N] as the reference builds them; the ABI takes B as [N, K], so each
+# B operand is transposed once.
+
+def _launch(a, b, c, config, dot_input_precision=None):
+    m, k = a.shape
+    n = b.shape[1]
+    b_nk = _once(b, lambda t: t.t().contiguous())
+    code = {torch.bfloat16: 0, torch.float16: 1, torch.float64: 4, torch.int8: 5}[a.dtype] \
+        if a.dtype != torch.float32 else (2 if dot_input_precision == "tf32" else 3)
+    _check(_lib.tcb_gemm(code, a.data_ptr(), b_nk.data_ptr(), None, None, c.data_ptr(),
+                         m, n, k, 0, None, _stream()))
