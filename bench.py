@@ -13,6 +13,12 @@ coordination over gloo), times exactly K steps with CUDA events between
 barriers, takes the max over ranks and prints one JSON line on rank 0.
 `--impl reference` times the reference's CPU path for the same workload
 (a host copy of the buffer, restated in oracle/tcb_oracle.c) on rank 0.
+
+After the copy's timed region the same line gains `rows`: every other
+configuration of the benchmark's table (tensor probes, vector chains, the MX
+FP4 8192^3 GEMM), each validated, timed with its own CUDA events and stamped
+with the SM clock sampled while it ran (baseline_rows.py); `--no-rows` skips
+them.
 """
 
 from __future__ import annotations
@@ -53,6 +59,8 @@ def parse_args():
     parser.add_argument("--cpu-seconds", type=float, default=10.0,
                         help="CPU-baseline sample duration")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-rows", action="store_true",
+                        help="skip the per-configuration rows measured after the copy")
     return parser.parse_args()
 
 
@@ -159,21 +167,29 @@ def run_ours(args):
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=device, generator=gen)
     dst = torch.zeros_like(src)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
     stream = torch.cuda.current_stream()
 
     def step():
-        _native.copy(src, dst, nbytes, variant, args.blocks, threads, stream)
+        _native.copy(src, dst, nbytes, variant, args.blocks, threads, stream, status=status)
+
+    def check(when):
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise AssertionError(f"copy kernel reported {_native.strerror(int(status.item()))} "
+                                 f"({when})")
+        if not torch.equal(src, dst):
+            raise AssertionError(f"copy validation failed: dst != src ({when})")
 
     step()
-    torch.cuda.synchronize()
-    if not torch.equal(src, dst):
-        raise AssertionError("copy validation failed: dst != src")
+    check("first launch")
     dst.zero_()
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
-    if not torch.equal(src, dst):
-        raise AssertionError("copy validation failed after warmup")
+    check("after warmup")
+    # The timed steps must rebuild dst themselves: a step that did nothing would
+    # leave these zeros behind and fail the check after the timed region.
+    dst.zero_()
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(dist)
@@ -185,6 +201,7 @@ def run_ours(args):
         end.record(stream)
         torch.cuda.synchronize()
     clocks = sampler.summary()
+    check("after the timed steps")
     barrier(dist)
     local_ms = start.elapsed_time(end)
     ms = all_max(dist, local_ms)
@@ -245,7 +262,47 @@ def run_ours(args):
         if not torch.equal(host_src, host_dst):
             raise AssertionError("end-to-end copy mismatch")
         e2e_value = world * traffic * args.e2e_steps / (e2e_ms / 1e3) / 1e9
+
+        # What the link allows: each direction alone, the whole buffer in one
+        # pinned copy, best of two.  With both directions at full rate at once
+        # (PCIe is full duplex) an end-to-end step takes at least the slower
+        # of the two, which bounds the end-to-end figure above.
+        def one_way(copy):
+            begin, finish = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+            begin.record(stream)
+            copy()
+            finish.record(stream)
+            torch.cuda.synchronize()
+            return begin.elapsed_time(finish)
+
+        barrier(dist)
+        h2d_ms = all_max(dist, min(one_way(lambda: src.copy_(host_src, non_blocking=True))
+                                   for _ in range(2)))
+        d2h_ms = all_max(dist, min(one_way(lambda: host_dst.copy_(dst, non_blocking=True))
+                                   for _ in range(2)))
+        ceiling = world * traffic / (max(h2d_ms, d2h_ms) / 1e3) / 1e9
+        pcie = {"h2d_gbs": world * nbytes / (h2d_ms / 1e3) / 1e9,
+                "d2h_gbs": world * nbytes / (d2h_ms / 1e3) / 1e9,
+                "ceiling_gbs": ceiling, "pcie_frac": e2e_value / ceiling,
+                "basis": "each direction timed alone (pinned, whole buffer, best of 2, max "
+                         "over ranks); ceiling = both directions at once at those rates"}
         del host_src, host_dst
+
+    # The north-star table's own configurations, measured after (outside) the
+    # copy's timed region on every rank at once; rank 0 reports its rows and
+    # the sum over ranks.
+    rows = None
+    if not args.no_rows:
+        from triton_chip_benchmarks_b200 import baseline_rows
+        del src, dst
+        torch.cuda.empty_cache()
+        barrier(dist)
+        rows = baseline_rows.measure_rows(device, measured_peaks())
+        for row in rows.values():
+            total = all_sum(dist, row.get("value", 0.0) if row["status"] == "ok" else 0.0)
+            if world > 1:
+                row["aggregate_value"] = total
+        barrier(dist)
 
     if rank != 0:
         if dist is not None:
@@ -284,8 +341,9 @@ def run_ours(args):
                 "d2h_bytes_per_step": nbytes, "steps": args.e2e_steps,
                 "path": "pinned host -> device, tcb_copy, device -> pinned host, in "
                         f"{chunk >> 20} MiB chunks on three streams (both PCIe directions "
-                        "at once)"},
+                        "at once)", **({"pcie": pcie} if e2e_value is not None else {})},
         "gpu_launches": args.steps, "clocks": clocks,
+        "rows": rows,
     }
     print(json.dumps(line), flush=True)
     if dist is not None:
