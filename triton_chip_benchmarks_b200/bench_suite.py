@@ -106,30 +106,53 @@ def probe_device(args) -> None:
     write_json(args.output, {"status": "ok", "device": metadata, "results": []})
 
 
+# Statuses a child declares about the device or the benchmark (its exit code
+# does not turn them into errors), and statuses that carry a measured rate.
+_DECLARED_GAPS = ("unsupported", "not_implemented")
+_MEASURED = ("ok", "unverified")
+
+
+def _child_document(output: Path):
+    """(document, None) from the child's JSON, or (None, why it is unusable)."""
+    if not output.exists():
+        return None, "Benchmark did not write result JSON"
+    try:
+        document = json.loads(output.read_text())
+    except (OSError, ValueError) as exc:
+        return None, f"Invalid benchmark JSON: {exc}"
+    if not isinstance(document, dict):
+        return None, "Invalid benchmark JSON: expected a JSON object"
+    return document, None
+
+
+def _summarized(metric, args, document: dict) -> dict:
+    try:
+        row = summarize(metric, document)
+    except (ValueError, TypeError, AttributeError, KeyError) as exc:
+        return empty_metric(metric, "error", f"Invalid benchmark JSON: {exc}")
+    if args.quick and row["status"] in _MEASURED and metric.group != "Memory":
+        row["smoke_only"] = True
+    return row
+
+
 def conclude(metric, args, output: Path, returncode, failure: str | None = None):
-    """Table row from a finished child: its JSON, exit code, or the failure text."""
-    document = None
+    """Table row from a finished child: its JSON, exit code, or the failure text.
+
+    A child that could not run (`failure`) or left no usable JSON is an error.
+    A non-zero exit is an error whatever the child wrote, unless it declared a
+    capability gap; a rate it did write is kept as ``partial_measurement``.
+    """
     if failure is not None:
         return empty_metric(metric, "error", failure), None
-    if output.exists():
-        try:
-            document = json.loads(output.read_text())
-            if not isinstance(document, dict):
-                raise ValueError("expected a JSON object")
-            result = summarize(metric, document)
-            if args.quick and result["status"] in ("ok", "unverified") \
-                    and metric.group != "Memory":
-                result["smoke_only"] = True
-        except (OSError, ValueError, TypeError, AttributeError, KeyError) as exc:
-            result = empty_metric(metric, "error", f"Invalid benchmark JSON: {exc}")
-    else:
-        result = empty_metric(metric, "error", "Benchmark did not write result JSON")
-    if returncode and result["status"] not in ("unsupported", "not_implemented"):
-        partial = result if result["status"] in ("ok", "unverified") else None
-        result = empty_metric(metric, "error", f"Benchmark exited with code {returncode}; see log")
-        if partial is not None:
-            result["partial_measurement"] = partial
-    return result, document
+    document, problem = _child_document(output)
+    row = (empty_metric(metric, "error", problem) if document is None
+           else _summarized(metric, args, document))
+    if returncode and row["status"] not in _DECLARED_GAPS:
+        failed = empty_metric(metric, "error", f"Benchmark exited with code {returncode}; see log")
+        if row["status"] in _MEASURED:
+            failed["partial_measurement"] = row
+        row = failed
+    return row, document
 
 
 def run_metric(metric, args, directory: Path, runner=subprocess.run):

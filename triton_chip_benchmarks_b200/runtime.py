@@ -174,121 +174,184 @@ def _coarse_time_error(launches, elapsed_ms, needed_ms):
                         f"{elapsed_ms:g} ms, but at least {needed_ms:g} ms is needed")
 
 
-def _elapsed(api, start, end, submit, *, allow_zero=False):
-    start.record()
-    submit()
-    end.record()
-    api.synchronize()
-    ms = float(start.elapsed_time(end))
-    if not math.isfinite(ms) or ms < 0:
-        raise RuntimeError(f"Invalid device event time: {ms!r} ms")
-    if ms == 0 and not allow_zero:
-        raise _zero_time_error()
-    return ms
-
-
 def _grow(launches):
     return min(MAX_BATCH_LAUNCHES, launches * 2)
 
 
-def _calibrate(api, start, end, direct):
-    """Smallest doubling of the direct-launch batch that the timer resolves."""
-    launches, saw_zero = INITIAL_CALIBRATION_LAUNCHES, False
-    while True:
-        ms = _elapsed(api, start, end, lambda: direct(launches), allow_zero=True)
-        if ms > 0:
-            return (ms / launches, launches, launches if saw_zero else 1,
-                    ms * MIN_RESOLVED_EVENT_TICKS if saw_zero else 0.0)
-        if launches == MAX_BATCH_LAUNCHES:
-            raise _zero_time_error(launches)
-        saw_zero = True
-        launches = _grow(launches)
+class _BatchTimer:
+    """The batch-timing policy as a small phase machine.
+
+    Each phase is a method that does its device work and returns the name of
+    the next phase:
+
+    calibrate  direct batches of 5, 10, 20 ... launches until the event timer
+               reads a nonzero time; that gives the per-launch estimate and,
+               when a zero reading came first, a floor of 20 readings' worth
+               of time that every later batch must reach;
+    size       the batch that fills min(--batch-ms, --rep / --rounds), built
+               (one captured graph in graph mode) and made resolvable;
+    refine     up to two re-sizings toward that target, skipped once the
+               batch time lies within a factor of two of it;
+    warm       replays of the batch for --warmup ms;
+    recapture  the batch built and resolved once more after warm-up;
+    sample     max(--rounds, --rep / batch time) resolved batch times.  An
+               unresolved sample doubles the batch, rebuilds it and returns
+               to ``sample``, which starts over, so all samples share one
+               launch count.
+
+    A batch is "resolved" when it reads a nonzero time at or above the floor;
+    building doubles the launch count (up to MAX_BATCH_LAUNCHES) until it is.
+    """
+
+    REFINE_PASSES = 2
+
+    def __init__(self, fn, api, graph_class, args):
+        self.fn, self.api, self.graph_class, self.args = fn, api, graph_class, args
+        self.start = api.Event(enable_timing=True)
+        self.end = api.Event(enable_timing=True)
+        self.target_ms = min(args.batch_ms, args.rep / args.rounds)
+        self.floor_ms = 0.0
+        self.per_launch_ms = 0.0
+        self.calibration_launches = 0
+        self.min_launches = 1
+        self.refines_left = self.REFINE_PASSES
+        self.launches, self.submit, self.batch_ms = 0, None, 0.0
+        self.samples: list[float] = []
+
+    # ---------------------------------------------------------- device work
+    def _run_direct(self, count):
+        for _ in range(count):
+            self.fn()
+
+    def _read(self, submit) -> float:
+        """Device time of one submission (zero allowed: a coarse timer's reading)."""
+        self.start.record()
+        submit()
+        self.end.record()
+        self.api.synchronize()
+        ms = float(self.start.elapsed_time(self.end))
+        if not math.isfinite(ms) or ms < 0:
+            raise RuntimeError(f"Invalid device event time: {ms!r} ms")
+        return ms
+
+    def _build(self, count):
+        """A submission of `count` launches: a captured graph's replay, or direct."""
+        if self.graph_class is None:
+            return lambda: self._run_direct(count)
+        try:
+            graph = self.graph_class()
+            with self.api.graph(graph):
+                self._run_direct(count)
+        except NotImplementedError as exc:
+            raise GraphUnavailable(f"graph capture: {exc}") from exc
+        except RuntimeError as exc:
+            text = str(exc).lower()
+            if any(w in text for w in ("not supported", "unsupported", "not implemented")):
+                raise GraphUnavailable(f"graph capture: {exc}") from exc
+            raise
+        return graph.replay
+
+    def _resolved(self, ms: float) -> bool:
+        return ms > 0 and ms >= self.floor_ms
+
+    def _unresolvable(self, count, ms):
+        error = (_zero_time_error(count) if ms == 0
+                 else _coarse_time_error(count, ms, self.floor_ms))
+        return GraphUnavailable(f"graph timing: {error}") if self.graph_class else error
+
+    def _clamp(self, count: int) -> int:
+        return max(self.min_launches, min(MAX_BATCH_LAUNCHES, count))
+
+    def _resolve(self, count: int, zero_seen: bool = False) -> None:
+        """Build batches from `count` launches up, doubling, until one resolves."""
+        while True:
+            submit = self._build(count)
+            ms = self._read(submit)
+            if ms > 0 and zero_seen and self.floor_ms == 0:
+                self.floor_ms = ms * MIN_RESOLVED_EVENT_TICKS
+            if self._resolved(ms):
+                self.launches, self.submit, self.batch_ms = count, submit, ms
+                return
+            if count == MAX_BATCH_LAUNCHES:
+                raise self._unresolvable(count, ms)
+            zero_seen = zero_seen or ms == 0
+            count = _grow(count)
+
+    # --------------------------------------------------------------- phases
+    def calibrate(self) -> str:
+        launches, saw_zero = INITIAL_CALIBRATION_LAUNCHES, False
+        while True:
+            ms = self._read(lambda: self._run_direct(launches))
+            if ms > 0:
+                break
+            if launches == MAX_BATCH_LAUNCHES:
+                raise _zero_time_error(launches)
+            saw_zero, launches = True, _grow(launches)
+        self.per_launch_ms = max(ms / launches, 0.001)
+        self.calibration_launches = launches
+        if saw_zero:
+            self.min_launches = launches
+            self.floor_ms = ms * MIN_RESOLVED_EVENT_TICKS
+        return "size"
+
+    def size(self) -> str:
+        self._resolve(self._clamp(math.ceil(self.target_ms / self.per_launch_ms)))
+        return "refine"
+
+    def refine(self) -> str:
+        if self.refines_left == 0 or 0.5 * self.target_ms <= self.batch_ms <= 2 * self.target_ms:
+            return "warm"
+        resized = self._clamp(math.ceil(self.launches * self.target_ms / self.batch_ms))
+        if resized == self.launches:
+            return "warm"
+        self.refines_left -= 1
+        self._resolve(resized)
+        return "refine"
+
+    def warm(self) -> str:
+        for _ in range(max(1, math.ceil(self.args.warmup / self.batch_ms))):
+            self.submit()
+        self.api.synchronize()
+        return "recapture"
+
+    def recapture(self) -> str:
+        self._resolve(self.launches)
+        return "sample"
+
+    def sample(self) -> str:
+        wanted = max(self.args.rounds, math.ceil(self.args.rep / self.batch_ms))
+        self.samples = []
+        while len(self.samples) < wanted:
+            ms = self._read(self.submit)
+            if self._resolved(ms):
+                self.samples.append(ms)
+                continue
+            if self.launches == MAX_BATCH_LAUNCHES:
+                raise self._unresolvable(self.launches, ms)
+            self._resolve(_grow(self.launches), zero_seen=ms == 0)
+            return "sample"
+        return "done"
+
+    def run(self) -> list[float]:
+        phase = "calibrate"
+        while phase != "done":
+            phase = getattr(self, phase)()
+        return self.samples
 
 
 def _batch_samples(fn, args, api, use_graph):
+    """Per-launch times (batch time / launches) and the batch details."""
     graph_class, graph_name = _graph_class(api) if use_graph else (None, None)
     if use_graph and graph_class is None:
         raise GraphUnavailable("the device API exposes no graph capture")
     with _timed_stream(api):
-        start, end = api.Event(enable_timing=True), api.Event(enable_timing=True)
-
-        def direct(count):
-            for _ in range(count):
-                fn()
-
-        estimate, calibration_launches, min_launches, min_batch_ms = _calibrate(
-            api, start, end, direct)
-        estimate = max(estimate, 0.001)
-        target = min(args.batch_ms, args.rep / args.rounds)
-        launches = max(min_launches, min(MAX_BATCH_LAUNCHES, math.ceil(target / estimate)))
-
-        def make_submit(count):
-            if not use_graph:
-                return lambda: direct(count)
-            try:
-                graph = graph_class()
-                with api.graph(graph):
-                    direct(count)
-            except NotImplementedError as exc:
-                raise GraphUnavailable(f"graph capture: {exc}") from exc
-            except RuntimeError as exc:
-                text = str(exc).lower()
-                if any(w in text for w in ("not supported", "unsupported", "not implemented")):
-                    raise GraphUnavailable(f"graph capture: {exc}") from exc
-                raise
-            return graph.replay
-
-        def time_batch(count, *, zero_seen=False):
-            nonlocal min_batch_ms
-            while True:
-                submit = make_submit(count)
-                ms = _elapsed(api, start, end, submit, allow_zero=True)
-                if ms > 0 and zero_seen and min_batch_ms == 0:
-                    min_batch_ms = ms * MIN_RESOLVED_EVENT_TICKS
-                if ms > 0 and ms >= min_batch_ms:
-                    return count, submit, ms
-                if count == MAX_BATCH_LAUNCHES:
-                    error = (_zero_time_error(count) if ms == 0
-                             else _coarse_time_error(count, ms, min_batch_ms))
-                    if use_graph:
-                        raise GraphUnavailable(f"graph timing: {error}")
-                    raise error
-                zero_seen = zero_seen or ms == 0
-                count = _grow(count)
-
-        launches, submit, batch_ms = time_batch(launches)
-        for _ in range(2):
-            refined = max(min_launches,
-                          min(MAX_BATCH_LAUNCHES, math.ceil(launches * target / batch_ms)))
-            if refined == launches or 0.5 * target <= batch_ms <= 2 * target:
-                break
-            launches, submit, batch_ms = time_batch(refined)
-        for _ in range(max(1, math.ceil(args.warmup / batch_ms))):
-            submit()
-        api.synchronize()
-        launches, submit, batch_ms = time_batch(launches)
-        rounds = max(args.rounds, math.ceil(args.rep / batch_ms))
-        batches = []
-        while len(batches) < rounds:
-            ms = _elapsed(api, start, end, submit, allow_zero=True)
-            if ms > 0 and ms >= min_batch_ms:
-                batches.append(ms)
-                continue
-            if launches == MAX_BATCH_LAUNCHES:
-                error = (_zero_time_error(launches) if ms == 0
-                         else _coarse_time_error(launches, ms, min_batch_ms))
-                if use_graph:
-                    raise GraphUnavailable(f"graph timing: {error}")
-                raise error
-            # Restart with a larger batch so every sample shares one denominator.
-            launches, submit, batch_ms = time_batch(_grow(launches), zero_seen=ms == 0)
-            rounds = max(args.rounds, math.ceil(args.rep / batch_ms))
-            batches.clear()
-    return [ms / launches for ms in batches], {
-        "launches_per_batch": launches, "batch_samples_ms": batches,
+        timer = _BatchTimer(fn, api, graph_class, args)
+        batches = timer.run()
+    return [ms / timer.launches for ms in batches], {
+        "launches_per_batch": timer.launches, "batch_samples_ms": batches,
         "sample_count": len(batches), "measured_total_ms": sum(batches),
-        "graph_api": graph_name, "calibration_launches": calibration_launches,
-        "minimum_resolved_batch_ms": min_batch_ms,
+        "graph_api": graph_name, "calibration_launches": timer.calibration_launches,
+        "minimum_resolved_batch_ms": timer.floor_ms,
     }
 
 
@@ -314,20 +377,19 @@ def _measure(fn, args, api) -> dict:
     fn()  # first launch outside any capture and any sample
     api.synchronize()
     requested = args.timing
-    selected = "events" if requested == "events" else "graph"
+    # Graph batches first unless plain events were asked for; "auto" falls back
+    # to event batches when graph capture or graph timing is unavailable.
+    modes = {"events": ("events",), "graph": ("graph",), "auto": ("graph", "events")}[requested]
     fallback = None
-    if selected == "graph":
+    for selected in modes:
         try:
-            samples, details = _batch_samples(fn, args, api, use_graph=True)
+            samples, details = _batch_samples(fn, args, api, use_graph=selected == "graph")
+            break
         except (GraphUnavailable, NotImplementedError) as exc:
-            if requested == "graph":
+            if selected == modes[-1]:
                 raise
             api.synchronize()
             fallback = str(exc)
-            selected = "events"
-            samples, details = _batch_samples(fn, args, api, use_graph=False)
-    else:
-        samples, details = _batch_samples(fn, args, api, use_graph=False)
     if not samples or any(not math.isfinite(v) or v <= 0 for v in samples):
         raise RuntimeError("Invalid device timing; increase the workload or --rep")
     notice = f"Timing: {selected} via device events"

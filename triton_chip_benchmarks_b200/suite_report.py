@@ -64,101 +64,163 @@ def _rates(metric: Metric, row: dict):
     """(peak, median) of one result row in the metric's unit."""
     if metric.key == "memory_bandwidth":
         return row.get("peak_gbps"), row.get("gbps")
-    peak = row.get("peak_teraops_per_second")
-    median = row.get("median_teraops_per_second")
     suffix = "tops" if metric.precision == "int8" else "tflops"
-    return (row.get(f"peak_{suffix}") if peak is None else peak,
-            row.get(suffix) if median is None else median)
+    return (_first_set(row, "peak_teraops_per_second", f"peak_{suffix}"),
+            _first_set(row, "median_teraops_per_second", suffix))
+
+
+def _first_set(row: dict, *keys):
+    """The first of `keys` whose value in `row` is not None."""
+    return next((row[key] for key in keys if row.get(key) is not None), None)
+
+
+def _has_rates(metric: Metric, row) -> bool:
+    return (isinstance(row, dict) and row.get("status", "ok") == "ok"
+            and all(_is_rate(v) for v in _rates(metric, row)))
+
+
+def _peak_of(metric: Metric):
+    return lambda row: _rates(metric, row)[0]
 
 
 def _row_details(metric: Metric, row: dict) -> dict:
+    """Value, median, audit fields (the row's own over its compiled record) and
+    the configuration that produced them."""
     peak, median = _rates(metric, row)
-    details = {"value": peak, "median_value": median,
-               "smoke_only": bool(row.get("smoke_only", False))}
     compiled = row.get("compiled") or {}
-    for key in _DETAIL_KEYS:
-        if key in row or key in compiled:
-            details[key] = row.get(key, compiled.get(key))
-    details["configuration"] = {key: row[key] for key in _CONFIG_KEYS if key in row}
-    return details
+    audit = {key: compiled[key] for key in _DETAIL_KEYS if key in compiled}
+    audit.update((key, row[key]) for key in _DETAIL_KEYS if key in row)
+    return {"value": peak, "median_value": median,
+            "smoke_only": bool(row.get("smoke_only", False)), **audit,
+            "configuration": {key: row[key] for key in _CONFIG_KEYS if key in row}}
+
+
+# Why a measured rate is kept but marked unverified: per group, the first rule
+# whose test holds gives the reason; no rule holding means verified.
+def _tensor_unit_unknown(metric: Metric, d: dict) -> bool:
+    execution = d.get("execution_kind")
+    unit_known = execution == "simt" or (execution == "tensor"
+                                         and d.get("native_tensor_verified") is True)
+    return d.get("instruction_precision_verified") is not True or not unit_known
+
+
+def _vector_unverified(metric: Metric, d: dict) -> bool:
+    return d.get("native_arithmetic_verified") is not True
+
+
+_UNVERIFIED_RULES = {
+    "Tensor": (
+        (_tensor_unit_unknown,
+         "Measured matrix rate retained; native instruction precision or execution unit is "
+         "unverified"),
+    ),
+    "Vector": (
+        (lambda m, d: (_vector_unverified(m, d) and m.precision == "int8"
+                       and bool(d.get("includes_unpacking"))),
+         "Measured portable INT8-input path uses INT32 arithmetic and includes unpacking; "
+         "native INT8 execution is unverified"),
+        (_vector_unverified,
+         "Measured vector rate retained; native arithmetic instruction precision is unverified"),
+    ),
+}
 
 
 def _verification_reason(metric: Metric, details: dict) -> str | None:
-    """Why a measured rate is kept but marked unverified (None when verified)."""
-    if metric.group == "Tensor":
-        execution = details.get("execution_kind")
-        known = execution == "simt" or (execution == "tensor"
-                                        and details.get("native_tensor_verified") is True)
-        if details.get("instruction_precision_verified") is not True or not known:
-            return ("Measured matrix rate retained; native instruction precision or execution "
-                    "unit is unverified")
-    elif metric.group == "Vector" and details.get("native_arithmetic_verified") is not True:
-        if metric.precision == "int8" and details.get("includes_unpacking"):
-            return ("Measured portable INT8-input path uses INT32 arithmetic and includes "
-                    "unpacking; native INT8 execution is unverified")
-        return "Measured vector rate retained; native arithmetic instruction precision is unverified"
+    return next((reason for test, reason in _UNVERIFIED_RULES.get(metric.group, ())
+                 if test(metric, details)), None)
+
+
+# summarize() is a chain of stages; each returns the finished row or None to
+# hand the document on.  `view` carries what earlier stages derived.
+_DECLARED_STATUSES = ("unsupported", "not_implemented", "error", "unavailable")
+
+
+def _stage_declared(metric, document, view):
+    status = document.get("status")
+    if status in _DECLARED_STATUSES:
+        return {**empty_metric(metric), "status": status,
+                "reason": document.get("reason", status)}
     return None
 
 
-def summarize(metric: Metric, document: dict) -> dict:
-    """One table row from a child's declared status and validated measurement rows."""
-    result = empty_metric(metric)
-    status = document.get("status")
-    if status in ("unsupported", "not_implemented", "error", "unavailable"):
-        result.update(status=status, reason=document.get("reason", status))
-        return result
-    if metric.key == "memory_capacity":
-        capacity = document.get("device", {}).get("total_memory_bytes")
-        if _is_rate(capacity):
-            result.update(status="ok", value=capacity / 2**30, capacity_bytes=capacity,
-                          measurement_kind="reported_device_capacity")
-        else:
-            result.update(status="unavailable",
-                          reason="Backend did not report total memory capacity")
-        return result
+def _stage_capacity(metric, document, view):
+    if metric.key != "memory_capacity":
+        return None
+    capacity = document.get("device", {}).get("total_memory_bytes")
+    if not _is_rate(capacity):
+        return {**empty_metric(metric), "status": "unavailable",
+                "reason": "Backend did not report total memory capacity"}
+    return {**empty_metric(metric), "status": "ok", "value": capacity / 2**30,
+            "capacity_bytes": capacity, "measurement_kind": "reported_device_capacity"}
 
+
+def _stage_rows(metric, document, view):
     rows = document.get("results", [])
     if not isinstance(rows, list):
         return empty_metric(metric, "error", "Benchmark results must be a list")
-    successful = [row for row in rows if isinstance(row, dict)
-                  and row.get("status", "ok") == "ok"
-                  and all(_is_rate(v) for v in _rates(metric, row))]
-    if not successful:
-        rejected = [row for row in rows if isinstance(row, dict)]
-        unsupported = rejected and all(row.get("status") == "unsupported" for row in rejected)
-        reasons = list(dict.fromkeys(str(row.get("reason", "No valid throughput"))
-                                     for row in rejected))
-        return empty_metric(metric, "unsupported" if unsupported else "error",
-                            "; ".join(reasons)
-                            or "Benchmark produced no valid throughput measurements")
+    view["rows"] = [row for row in rows if isinstance(row, dict)]
+    view["valid"] = [row for row in rows if _has_rates(metric, row)]
+    if view["valid"]:
+        return None
+    rejected = view["rows"]
+    reasons = "; ".join(dict.fromkeys(str(row.get("reason", "No valid throughput"))
+                                      for row in rejected))
+    all_unsupported = bool(rejected) and all(row.get("status") == "unsupported"
+                                             for row in rejected)
+    return empty_metric(metric, "unsupported" if all_unsupported else "error",
+                        reasons or "Benchmark produced no valid throughput measurements")
 
-    if metric.key == "memory_bandwidth":
-        patterns = {}
-        for pattern in ("copy", "read"):
-            candidates = [row for row in successful if row.get("pattern") == pattern]
-            eligible = [row for row in candidates if row.get("peak_eligible") is True
-                        and not row.get("smoke_only", False)]
-            if candidates:
-                best = max(eligible or candidates, key=lambda row: _rates(metric, row)[0])
-                patterns[pattern] = _row_details(metric, best)
-        result["patterns"] = patterns
-        successful = [row for row in successful if row.get("pattern") == "copy"
-                      and row.get("peak_eligible") is True and not row.get("smoke_only", False)]
-        if not successful:
-            result.update(status="not_measured", reason=(
-                "No HBM-sized copy candidate: use a non-quick run with known L2 capacity "
-                "and buffers at least 4x L2; observed pattern rates remain in patterns"))
-            return result
 
-    best = max(successful, key=lambda row: _rates(metric, row)[0])
-    result.update(status="ok", **_row_details(metric, best))
+def _hbm_sized(row) -> bool:
+    return row.get("peak_eligible") is True and not row.get("smoke_only", False)
+
+
+def _stage_bandwidth(metric, document, view):
+    """Copy and read patterns are kept as details; only an HBM-sized copy row
+    may give the metric's value."""
+    if metric.key != "memory_bandwidth":
+        return None
+    patterns = {}
+    for pattern in ("copy", "read"):
+        rows = [row for row in view["valid"] if row.get("pattern") == pattern]
+        pool = [row for row in rows if _hbm_sized(row)] or rows
+        if pool:
+            patterns[pattern] = _row_details(metric, max(pool, key=_peak_of(metric)))
+    view["patterns"] = patterns
+    view["valid"] = [row for row in view["valid"]
+                     if row.get("pattern") == "copy" and _hbm_sized(row)]
+    if view["valid"]:
+        return None
+    return {**empty_metric(metric), "patterns": patterns, "status": "not_measured",
+            "reason": "No HBM-sized copy candidate: use a non-quick run with known L2 capacity "
+                      "and buffers at least 4x L2; observed pattern rates remain in patterns"}
+
+
+def _stage_best(metric, document, view):
+    valid = view["valid"]
+    result = {**empty_metric(metric), **({"patterns": view["patterns"]}
+                                         if "patterns" in view else {}),
+              "status": "ok", **_row_details(metric, max(valid, key=_peak_of(metric)))}
     if document.get("arguments", {}).get("quick") and metric.group != "Memory":
         result["smoke_only"] = True
     reason = _verification_reason(metric, result)
     if reason:
         result.update(status="unverified", reason=reason)
-    result["successful_configurations"] = len(successful)
+    result["successful_configurations"] = len(valid)
     return result
+
+
+_SUMMARY_STAGES = (_stage_declared, _stage_capacity, _stage_rows, _stage_bandwidth, _stage_best)
+
+
+def summarize(metric: Metric, document: dict) -> dict:
+    """One table row from a child's declared status and validated measurement rows."""
+    view: dict = {}
+    for stage in _SUMMARY_STAGES:
+        result = stage(metric, document, view)
+        if result is not None:
+            return result
+    raise AssertionError("the last summary stage always returns a row")
 
 
 _RUN_KEYS = ("command", "source_json", "log_file", "returncode", "device_index", "window",
@@ -231,23 +293,34 @@ def format_per_gpu(results: list[dict]) -> str:
     return "\n".join(lines)
 
 
+# The table: (header, width/alignment, cell) per column; the last column is
+# unpadded.  Notes follow the table, one per matching (test, text) rule.
+_TABLE_COLUMNS = (
+    ("Metric", "<20", lambda item: item["metric"]),
+    ("Peak / capacity", ">17",
+     lambda item: "-" if item.get("value") is None else f"{item['value']:.3f}"),
+    ("Median", ">12",
+     lambda item: "-" if item.get("median_value") is None else f"{item['median_value']:.3f}"),
+    ("Unit", "<8", lambda item: item["unit"]),
+    ("Status", "", lambda item: item["status"]),
+)
+_TABLE_RULE_WIDTH = 86
+_TABLE_NOTES = (
+    (lambda item: item.get("reason"), lambda item: item["reason"]),
+    (lambda item: item.get("smoke_only"), lambda item: "smoke test; not a peak result"),
+    (lambda item: item.get("execution_kind") == "simt",
+     lambda item: "measured matrix rate using SIMT scalar/vector instructions (no native "
+                  "tensor MMA)"),
+)
+
+
 def format_table(results: list[dict]) -> str:
     """One line per requested metric, including missing results, then notes."""
-    lines = [f"{'Metric':<20} {'Peak / capacity':>17} {'Median':>12} {'Unit':<8} Status",
-             "-" * 86]
-    notes = []
-    for item in results:
-        value = "-" if item.get("value") is None else f"{item['value']:.3f}"
-        median = "-" if item.get("median_value") is None else f"{item['median_value']:.3f}"
-        lines.append(f"{item['metric']:<20} {value:>17} {median:>12} "
-                     f"{item['unit']:<8} {item['status']}")
-        if item.get("reason"):
-            notes.append(f"{item['metric']}: {item['reason']}")
-        if item.get("smoke_only"):
-            notes.append(f"{item['metric']}: smoke test; not a peak result")
-        if item.get("execution_kind") == "simt":
-            notes.append(f"{item['metric']}: measured matrix rate using SIMT scalar/vector "
-                         "instructions (no native tensor MMA)")
-    if notes:
-        lines.extend(("", *notes))
-    return "\n".join(lines)
+    def line(cells):
+        return " ".join(f"{cell:{spec}}" for cell, (_, spec, _) in zip(cells, _TABLE_COLUMNS))
+
+    lines = [line([header for header, _, _ in _TABLE_COLUMNS]), "-" * _TABLE_RULE_WIDTH]
+    lines += [line([cell(item) for _, _, cell in _TABLE_COLUMNS]) for item in results]
+    notes = [f"{item['metric']}: {text(item)}" for item in results
+             for test, text in _TABLE_NOTES if test(item)]
+    return "\n".join(lines + (["", *notes] if notes else []))
