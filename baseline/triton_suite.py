@@ -1,0 +1,92 @@
+#!/usr/bin/env python3
+"""Run the reference suite's own Triton kernels, unmodified, on a B200.
+
+The reference suite (huangyiqun/triton_chip_benchmarks) is plain Python +
+Triton, driven through FlagGems.  This script runs its ``bench_suite.py`` as
+is, with ``baseline/flag_gems`` (a FlagGems stand-in over torch.cuda) on the
+import path, so its 17-row table can be set beside this repository's on the
+same GPU.
+
+    python baseline/triton_suite.py --install /path/to/reference   # once, here
+    python baseline/triton_suite.py --output out/triton_suite.json [suite flags]
+
+``--install`` copies the reference's top-level Python modules into
+``baseline/_ref`` (git-ignored; it travels with the working tree to the GPU
+box).  Every other flag goes to the reference's ``bench_suite.py`` unchanged
+(``--device``, ``--timing``, ``--quick``, ``--metrics``, ``--timeout`` ...).
+With ``--compare OURS.json`` the two tables are printed side by side.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import shutil
+import subprocess
+import sys
+
+HERE = Path(__file__).resolve().parent
+REF = HERE / "_ref"
+
+
+def install(source: Path) -> None:
+    modules = sorted(source.glob("*.py"))
+    if not any(m.name == "bench_suite.py" for m in modules):
+        raise SystemExit(f"{source} does not hold the reference suite (no bench_suite.py)")
+    REF.mkdir(exist_ok=True)
+    for module in modules:
+        shutil.copy2(module, REF / module.name)
+    print(f"copied {len(modules)} modules into {REF}")
+
+
+def run(suite_args: list[str], output: Path) -> int:
+    if not (REF / "bench_suite.py").exists():
+        raise SystemExit(f"{REF} is empty; run with --install <reference checkout> first")
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join(
+        [str(HERE), str(REF)] + ([env["PYTHONPATH"]] if env.get("PYTHONPATH") else []))
+    output.parent.mkdir(parents=True, exist_ok=True)
+    command = [sys.executable, "-u", str(REF / "bench_suite.py"), "--output", str(output),
+               *suite_args]
+    print("running:", " ".join(command), flush=True)
+    return subprocess.run(command, env=env, check=False).returncode
+
+
+def compare(reference: Path, ours: Path) -> None:
+    theirs = {r["metric"]: r for r in json.loads(reference.read_text())["results"]}
+    mine = {r["metric"]: r for r in json.loads(ours.read_text())["results"]}
+    print(f"\n{'metric':<20} {'Triton (reference)':>22} {'libtcb':>22} {'ratio':>8}")
+    for key, row in mine.items():
+        other = theirs.get(key, {})
+
+        def cell(r):
+            v = r.get("value")
+            return f"{v:.2f} {r.get('status', '')}" if v is not None else r.get("status", "-")
+
+        ratio = (f"{row['value'] / other['value']:.2f}" if row.get("value") and other.get("value")
+                 else "-")
+        print(f"{key:<20} {cell(other):>22} {cell(row):>22} {ratio:>8}")
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--install", type=Path, metavar="REFERENCE",
+                        help="copy the reference suite's modules into baseline/_ref and exit")
+    parser.add_argument("--output", type=Path, default=Path("gpurun_out/triton_suite.json"))
+    parser.add_argument("--compare", type=Path, metavar="OURS",
+                        help="print this repository's table JSON beside the reference's")
+    args, suite_args = parser.parse_known_args()
+    if args.install is not None:
+        install(args.install)
+        return 0
+    rc = run(suite_args, args.output)
+    if args.compare is not None and args.output.exists():
+        compare(args.output, args.compare)
+    return rc
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
