@@ -44,10 +44,26 @@ using namespace gemm_detail;
 
 }  // namespace
 
-int gemm_pair_launch(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_c,
-                     const GemmArgs& args, int pairs, const DeviceFacts& facts,
-                     cudaStream_t stream);
+int gemm_pair_run(const void* A, const void* B, const void* SA, const void* SB, void* C, int M,
+                  int N, int K, int blocks, int* status, uint32_t idesc, const DeviceFacts& facts,
+                  cudaStream_t stream);
 int gemm_pair_info(tcb_kernel_info_t* out);
+
+// cuTensorMapEncodeTiled from the driver, resolved once (thread-safe static
+// initialisation); null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    clear_stale_error();
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
+  return fn;
+}
 
 namespace {
 
@@ -370,24 +386,9 @@ uint32_t gemm_idesc(int kind, int mma_m = 128) {
   return d | c_fmt << 4 | ab << 7 | ab << 10;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 gemm_encode_fn() {
-  // Resolved once (thread-safe static initialisation).
-  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    clear_stale_error();
-    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
-  }();
-  return fn;
-}
-
 int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes,
              int box_rows) {
-  auto fn = gemm_encode_fn();
+  auto fn = tensor_map_encoder();
   if (fn == nullptr) return TCB_ERR_DEVICE;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
@@ -403,7 +404,7 @@ int gemm_map(CUtensorMap* map, const void* base, long long rows, long long row_b
 // C [M][N] of 32-bit elements, 32 x 32 boxes in the SWIZZLE_128B layout the
 // epilogue stages; needs N % 4 == 0 (16-byte row pitch) and a 16-byte base.
 int gemm_map_c(CUtensorMap* map, void* base, int rows, int cols) {
-  auto fn = gemm_encode_fn();
+  auto fn = tensor_map_encoder();
   if (fn == nullptr) return TCB_ERR_DEVICE;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
@@ -537,31 +538,8 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   const long long kbytes = kbits / 8;
   if (kind == gMXF4 && M > 128) {
     // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of A and of B.
-    CUtensorMap map_a, map_b;
-    if ((rc = gemm_map(&map_a, A, M, kbytes, 128)) != TCB_OK) return rc;
-    if ((rc = gemm_map(&map_b, B, N, kbytes, 128)) != TCB_OK) return rc;
-    GemmArgs args;
-    args.sa = static_cast<const uint8_t*>(SA);
-    args.sb = static_cast<const uint8_t*>(SB);
-    args.c = static_cast<uint32_t*>(C);
-    args.status = status_dev;
-    args.m = M;
-    args.n = N;
-    args.kbytes = static_cast<int>(kbytes);
-    args.kgroups = K / 32;
-    args.tiles_m = (M + 255) / 256;
-    args.tiles_n = (N + kTileN - 1) / kTileN;
-    args.kblocks = static_cast<int>((kbytes + kBlockBytes - 1) / kBlockBytes);
-    args.vec_store = N % 4 == 0 && aligned(C, 16);
-    CUtensorMap map_c{};
-    args.tma_store = args.vec_store && gemm_map_c(&map_c, C, M, N) == TCB_OK;
-    args.idesc = gemm_idesc(kind, 256);
-    const int tiles = args.tiles_m * args.tiles_n;
-    int pairs = blocks > 0 ? blocks / 2 : facts.sm_count / 2;
-    if (pairs < 1) pairs = 1;
-    if (pairs > tiles) pairs = tiles;
-    return gemm_pair_launch(map_a, map_b, map_c, args, pairs, facts,
-                            reinterpret_cast<cudaStream_t>(stream));
+    return gemm_pair_run(A, B, SA, SB, C, M, N, K, blocks, status_dev, gemm_idesc(kind, 256),
+                         facts, reinterpret_cast<cudaStream_t>(stream));
   }
   const int halves = gemm_halves(kind, M, N, facts.sm_count);
   const int tile_m = 128 * halves;

@@ -68,11 +68,16 @@ struct GemmArgs {
   uint32_t idesc;
 };
 
+// Bounded wait on an mbarrier phase.  `sleep_ns` > 0 backs off between polls
+// (for roles whose wait is not on the critical path: many warps polling in a
+// tight loop take issue slots from the warps that feed the tensor cores).
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
-                                              volatile int* abort_flag, int* status) {
+                                              volatile int* abort_flag, int* status,
+                                              unsigned sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
+    if (sleep_ns) __nanosleep(sleep_ns);
     if (*abort_flag) return false;
     if (globaltimer_ns() - start > kWaitTimeoutNs) {
       *abort_flag = 1;
