@@ -187,12 +187,16 @@ long long tcb_mx_scales_packed_bytes(int rows, int groups);
 
 /* Rearrange E8M0 scales src [rows][groups] (row-major, one byte per 32 K
  * elements) into the layout tcb_gemm reads: rows padded to a multiple of 256
- * and groups to a multiple of 8 with the unit scale 127, then for each block
- * of 128 rows and each 8 groups (256 K elements) 128 rows x 8 bytes
- * contiguous: dst[((r/128)*(groups_p/8) + g/8)*1024 + (r%128)*8 + g%8] =
- * src[r*groups + g].  dst holds tcb_mx_scales_packed_bytes(rows, groups)
- * bytes, 16-byte aligned.  Run once per scale tensor (data preparation, not
- * part of the GEMM).  No counterpart in the reference. */
+ * and groups to a multiple of 8 with the unit scale 127, then one 1 KB block
+ * per 128 rows and 8 groups, in two 512-byte halves (groups 0-3 and 4-7) of
+ * 32 x 16 bytes, lane l = r % 32 holding the four groups of rows l, 32+l,
+ * 64+l, 96+l:
+ * dst[((r/128)*(groups_p/8) + g/8)*1024 + (g%8/4)*512 + (r%32)*16
+ *     + (r%128/32)*4 + g%4] = src[r*groups + g].
+ * Each half is the shared-memory source of one tensor-memory copy
+ * (tcgen05.cp.32x128b.warpx4).  dst holds tcb_mx_scales_packed_bytes(rows,
+ * groups) bytes, 16-byte aligned.  Run once per scale tensor (data
+ * preparation, not part of the GEMM).  No counterpart in the reference. */
 int tcb_mx_scales_pack(const void *src, void *dst, int rows, int groups, tcb_stream_t stream);
 
 /* MX FP4 GEMM that allocates nothing, for callers that cannot allocate device

@@ -49,15 +49,19 @@ def pack_mx_scales(scales: np.ndarray) -> np.ndarray:
     """The GEMM's packed E8M0 layout (this build's own format, flat uint8).
 
     Rows are padded to a multiple of 256 and groups to a multiple of 8 with the
-    unit scale 127; then out[((r//128)*(groups_p//8) + g//8)*1024 + (r%128)*8 + g%8]
-    = scales[r, g].
+    unit scale 127; then, per 128 rows and 8 groups, a 1 KB block of two
+    512-byte halves (groups 0-3, 4-7) in which lane l = r % 32 holds the four
+    groups of rows l, 32+l, 64+l, 96+l:
+    out[((r//128)*(groups_p//8) + g//8)*1024 + (g%8//4)*512 + (r%32)*16
+        + (r%128//32)*4 + g%4] = scales[r, g].
     """
     rows, groups = scales.shape
     rows_p, groups_p = -(-rows // 256) * 256, -(-groups // 8) * 8
     padded = np.full((rows_p, groups_p), E8M0_UNIT_SCALE, dtype=np.uint8)
     padded[:rows, :groups] = scales
-    s = padded.reshape(rows_p // 128, 128, groups_p // 8, 8)
-    return np.ascontiguousarray(s.transpose(0, 2, 1, 3)).reshape(-1)
+    # axes: row block, row quarter j, lane l, group block, half h, group b
+    s = padded.reshape(rows_p // 128, 4, 32, groups_p // 8, 2, 4)
+    return np.ascontiguousarray(s.transpose(0, 3, 4, 2, 1, 5)).reshape(-1)
 
 
 def peak_tolerance(dtype: str, block_k: int, iterations: int) -> float:

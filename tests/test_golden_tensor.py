@@ -158,14 +158,21 @@ def test_fp64_probe_verdicts():
         assert np.array_equal(observed, expected) == v["accepted"], v
 
 
+def _packed_offset(r: int, g: int, groups_p: int) -> int:
+    return (((r // 128) * (groups_p // 8) + g // 8) * 1024 + (g % 8 // 4) * 512 + (r % 32) * 16
+            + (r % 128 // 32) * 4 + g % 4)
+
+
 def test_pack_mx_scales_layout():
-    """Packed scale layout: row r, group g at ((r//128)*(G//8) + g//8)*1024 + (r%128)*8 + g%8."""
+    """Packed scale layout: 1 KB per 128 rows x 8 groups, two 32 x 16-byte halves."""
     rows, groups = 256, 16
     src = np.arange(rows * groups, dtype=np.int64).reshape(rows, groups) % 251
     packed = oracle_tensor.pack_mx_scales(src.astype(np.uint8)).reshape(-1)
-    for r, g in ((0, 0), (5, 3), (127, 7), (128, 8), (200, 13), (255, 15)):
-        offset = ((r // 128) * (groups // 8) + g // 8) * 1024 + (r % 128) * 8 + g % 8
-        assert packed[offset] == src[r, g] % 256
+    for r, g in ((0, 0), (5, 3), (127, 7), (128, 8), (200, 13), (255, 15), (33, 4), (97, 6)):
+        assert packed[_packed_offset(r, g, groups)] == src[r, g] % 256
+    # Lane l's 16 bytes of a half are rows l, 32+l, 64+l, 96+l, four groups each.
+    half = packed[512:1024].reshape(32, 4, 4)
+    assert np.array_equal(half[7, 2], src[64 + 7, 4:8] % 256)
 
 
 def test_pack_mx_scales_padding():
@@ -175,8 +182,10 @@ def test_pack_mx_scales_padding():
     assert packed.size == 256 * 24
     assert np.count_nonzero(packed == 3) == 130 * 17
     assert np.all(packed[packed != 3] == oracle_tensor.E8M0_UNIT_SCALE)
-    # row 129, group 16 -> block (1, 2): offset ((1*3 + 2)*1024) + 1*8 + 0
-    assert packed[(1 * 3 + 2) * 1024 + 8] == 3 and packed[(1 * 3 + 2) * 1024 + 8 + 1] == 127
+    # row 129 (lane 1 of quarter 0, row block 1), groups 16 and 17 (block 2, half 0)
+    assert packed[_packed_offset(129, 16, 24)] == 3
+    assert packed[(1 * 3 + 2) * 1024 + 1 * 16 + 0] == 3
+    assert packed[_packed_offset(129, 17, 24)] == 127
 
 
 def test_gemm_inputs_pad_unaligned_k():

@@ -37,24 +37,35 @@ __device__ __forceinline__ uint32_t sf_idesc(uint32_t idesc, int k) {
   return idesc | (id << 29) | (id << 4);  // A scale factor ID [29,31), B [4,6)
 }
 
-// Stage scale records (8 bytes = groups 0-7 of one row's K block) into tensor
-// memory: word x covers K steps 0-1, word y K steps 2-3, as staged.
-__device__ __forceinline__ void write_scale_slot(uint32_t lane_col0, const uint2 (&fa)[4],
-                                                 const uint2 (&fb)[kTileN / 32]) {
+// Scales of one K block into the tensor-memory slot at column `sf`, by
+// tcgen05.cp from shared memory.  `sa`, `sb0` and `sb1` are the 1 KB packed
+// blocks (tcb_mx_scales_pack layout) of A's 128 rows and of B rows 0-127 and
+// 128-255, as shared-memory addresses in 16-byte units.  Half kp (512 bytes)
+// of a block is the 32 x 16-byte copy source for the word of K steps 2kp and
+// 2kp+1: lane l's 16 bytes hold the four scales of rows l, 32+l, 64+l and
+// 96+l, so column j of the copy holds rows 32j+l, the layout that sf_cols_a
+// and sf_cols_b address.  PAIR: issued by a pair's leader (cta_group::2).
+template <bool PAIR>
+__device__ __forceinline__ void copy_scale_block(uint32_t sf, uint32_t sa, uint32_t sb0,
+                                                 uint32_t sb1) {
+  const uint64_t d = smem_desc(0, 128, 128, 0);
 #pragma unroll
   for (int kp = 0; kp < 2; ++kp) {
-    uint32_t va[4], vb[kTileN / 32];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) va[j] = kp == 0 ? fa[j].x : fa[j].y;
-#pragma unroll
-    for (int j = 0; j < kTileN / 32; ++j) vb[j] = kp == 0 ? fb[j].x : fb[j].y;
-    tmem_st_4cols(lane_col0 + kp * kSfPairCols, va);
-    tmem_st_8cols(lane_col0 + kp * kSfPairCols + 4, vb);
+    const uint32_t col = sf + static_cast<uint32_t>(kp * kSfPairCols);
+    const uint32_t half = static_cast<uint32_t>(kp * (512 >> 4));
+    if constexpr (PAIR) {
+      tmem_cp_32x128b_x4_pair(col, d | (sa + half));
+      tmem_cp_32x128b_x4_pair(col + 4, d | (sb0 + half));
+      tmem_cp_32x128b_x4_pair(col + 8, d | (sb1 + half));
+    } else {
+      tmem_cp_32x128b_x4(col, d | (sa + half));
+      tmem_cp_32x128b_x4(col + 4, d | (sb0 + half));
+      tmem_cp_32x128b_x4(col + 8, d | (sb1 + half));
+    }
   }
 }
 constexpr int kTmemCols = 512;
 constexpr int kEpilogueWarps = 4;
-constexpr int kScaleWarps = 4;
 
 struct GemmArgs {
   const uint8_t* sa;  // [M][K/32] E8M0 (MX FP4)

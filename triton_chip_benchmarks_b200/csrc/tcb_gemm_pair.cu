@@ -24,7 +24,11 @@
 // operand producer, the MMA waited on them 9-10 % of its time, and a single
 // thread issuing five TMA operations per stage (about 100 cycles each) could
 // not keep three operand stages in flight.  (Measured on 8192^3: 3.9 to 5.8
-// PFLOP/s across these steps; the breakdown is in the design notes.)
+// PFLOP/s across these steps; the breakdown is in the design notes.)  Copying
+// the scales with tcgen05.cp from the MMA thread instead (six per K block,
+// ordered with the MMAs, as the single-CTA kernel does) removes the writer
+// warps and their wait, but each copy takes tensor-pipe time: 5.3 against
+// 5.9 PFLOP/s here.
 //
 // The accumulator (128 rows x 256 fp32 columns per CTA) is drained by 16
 // epilogue warps that each load their whole 32 x 64 slice into registers and
@@ -385,8 +389,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     if (lane == 0) bulk_wait_group_all();  // C stores complete before the CTA retires
   } else if (warp < kPairLoaderWarp) {
     // ------------------------------------------------------ scale writers
-    // Lane l takes rows 32j+l (8 bytes each) of each staged K block's scales
-    // and writes them into this CTA's tensor-memory slot (two K steps per word).
+    // Lane l writes rows 32j+l of each staged K block's scales into this
+    // CTA's tensor-memory slot (two K steps per word).
     const int quarter = warp & 3;
     const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
     int sb = 0;  // stage block of `it` within its tile
@@ -399,19 +403,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         break;
       const int nkb = min(kPairPanels, args.kblocks - sb * kPairPanels);
       if (++sb == stage_blocks) sb = 0;
-      const uint8_t* ss = smem + kPairSlotOffset + slot * kPairSlotBytes + lane * 8;
+      // Packed layout: lane l's 16 bytes of each 512-byte half are exactly its
+      // words for the four A columns (rows l, 32+l, 64+l, 96+l), and those of
+      // B rows 0-127 and 128-255 for the eight B columns.
+      const uint8_t* ss = smem + kPairSlotOffset + slot * kPairSlotBytes + lane * 16;
 #pragma unroll
       for (int q = 0; q < kPairPanels; ++q) {
         if (q >= nkb) break;
-        uint2 fa[4], fb[kTileN / 32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) fa[j] = *reinterpret_cast<const uint2*>(ss + q * 1024 + 256 * j);
-#pragma unroll
-        for (int j = 0; j < kTileN / 32; ++j)
-          fb[j] = *reinterpret_cast<const uint2*>(ss + (1 + (j >> 2)) * kPairPanels * 1024 +
-                                                  q * 1024 + 256 * (j & 3));
-        write_scale_slot(lane_base + static_cast<uint32_t>(slot * kPairSfCols + q * kSfStageCols),
-                         fa, fb);
+        for (int kp = 0; kp < 2; ++kp) {
+          const uint8_t* h = ss + q * 1024 + kp * 512;
+          const uint4 a = *reinterpret_cast<const uint4*>(h);
+          const uint4 b0 = *reinterpret_cast<const uint4*>(h + kPairPanels * 1024);
+          const uint4 b1 = *reinterpret_cast<const uint4*>(h + 2 * kPairPanels * 1024);
+          const uint32_t va[4] = {a.x, a.y, a.z, a.w};
+          const uint32_t vb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const uint32_t col = lane_base + static_cast<uint32_t>(slot * kPairSfCols +
+                                                                 q * kSfStageCols + kp * kSfPairCols);
+          tmem_st_4cols(col, va);
+          tmem_st_8cols(col + 4, vb);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
