@@ -45,13 +45,14 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
+    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="ldg128")
     parser.add_argument("--buffer-mib", type=int, default=BUFFER_BYTES >> 20,
                         help="buffer size (default: the 4 GiB workload; smaller only for profiling)")
-    parser.add_argument("--threads", type=int, default=512, help="CTA size of the ldg128 kernel")
+    parser.add_argument("--threads", type=int, default=768, help="CTA size of the ldg128 kernel")
     parser.add_argument("--stages", type=int, default=0,
                         help="bulk kernel ring depth in 32 KiB chunks (0: library default)")
-    parser.add_argument("--blocks", type=int, default=0, help="CTAs (0: library default)")
+    parser.add_argument("--blocks", type=int, default=0,
+                        help="CTAs (0: library default, one per piece for ldg128)")
     parser.add_argument("--e2e-chunk-mib", type=int, default=256,
                         help="chunk of the end-to-end pipeline (default: 256 MiB)")
     parser.add_argument("--e2e-steps", type=int, default=3,
@@ -333,7 +334,8 @@ def run_ours(args):
                    "bytes_per_step": traffic, "kernel": kernel_name,
                    "threads_per_cta": threads if args.variant == "ldg128" else 32,
                    "bulk_ring_stages": threads if args.variant == "bulk" else None,
-                   "ctas": args.blocks or "library default",
+                   "ctas": args.blocks or ("one per 24 KiB piece" if args.variant == "ldg128"
+                                           and threads == 768 else "library default"),
                    "l2": "no flush: inputs (4 GiB) larger than the 126 MB L2",
                    "parallelism": f"replicas x{world} (no collective)"},
         "roofline": roofline, "cpu_baseline": cpu,

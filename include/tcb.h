@@ -70,13 +70,15 @@ typedef struct tcb_device_props {
 int tcb_device_query(int device, tcb_device_props *out);
 
 /* --------------------------------------------------------- copy / read */
-#define TCB_COPY_LDG128 0 /* persistent grid-stride 128-bit loads/stores */
+#define TCB_COPY_LDG128 0 /* 128-bit loads/stores, one CTA per piece (or grid-stride) */
 #define TCB_COPY_BULK 1   /* bulk-copy engine: global -> shared -> global, one lane per CTA */
 
 /* dst[0:bytes) = src[0:bytes).  Any byte count and alignment is accepted;
  * both kernels need 16-byte aligned pointers and otherwise fall back to a byte
  * loop.  blocks = 0 selects the tuned grid for the variant.  For LDG128,
- * `threads` is the CTA size (0: 512).  For BULK the CTA is one warp and
+ * `threads` is the CTA size (0: 768) and each CTA copies a piece of
+ * threads x 32 bytes; blocks = 0 launches one CTA per piece, a smaller
+ * positive `blocks` walks the pieces grid-stride.  For BULK the CTA is one warp and
  * `threads` is the depth of the shared-memory ring in 32 KiB chunks (2..8,
  * 0: 2; the default grid is 2 CTAs per SM). src and dst must not overlap.
  * A bulk-copy ring wait that runs out writes TCB_ERR_TIMEOUT into

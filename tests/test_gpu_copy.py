@@ -34,14 +34,30 @@ def test_copy_misaligned_falls_back(cuda, native, offset):
     assert torch.equal(out[offset:offset + n], base[offset:offset + n])
 
 
-@pytest.mark.parametrize("threads", [256, 1024])
-def test_copy_thread_configs(cuda, native, threads):
-    n = (32 << 20) + 16 * 7
+@pytest.mark.parametrize("threads,blocks", [(256, 0), (768, 0), (1024, 0), (768, 7), (96, 1)])
+def test_copy_thread_configs(cuda, native, threads, blocks):
+    """One CTA per piece (blocks 0) and grid-stride grids, with a ragged piece and tail."""
+    n = (32 << 20) + 16 * 7 + 5
     src = torch.randint(0, 256, (n,), dtype=torch.uint8, device=cuda)
     dst = torch.zeros_like(src)
-    native.copy(src, dst, n, native.COPY_LDG128, 0, threads)
+    native.copy(src, dst, n, native.COPY_LDG128, blocks, threads)
     torch.cuda.synchronize()
     assert torch.equal(src, dst)
+
+
+@pytest.mark.parametrize("offset,extra", [(0, 16), (16, 0), (16, 48), (32, 8), (0, 15)])
+def test_copy_piece_alignment(cuda, native, offset, extra):
+    """256-bit vectors (both pointers 32-byte aligned), two 16-byte vectors
+    (16-byte aligned), an odd count of 16-byte vectors and a byte tail; bytes
+    outside the range stay untouched."""
+    n = (8 << 20) + 768 * 32 * 3 + extra
+    gen = torch.Generator().manual_seed(offset + extra)
+    base = torch.randint(0, 256, (n + 128,), dtype=torch.uint8, generator=gen).to(cuda)
+    out = torch.zeros_like(base)
+    native.copy(base[offset:], out[offset:], n)
+    torch.cuda.synchronize()
+    assert torch.equal(out[offset:offset + n], base[offset:offset + n])
+    assert int(out[:offset].count_nonzero()) == 0 and int(out[offset + n:].count_nonzero()) == 0
 
 
 def test_copy_matches_oracle_copy(cuda, native):

@@ -8,8 +8,9 @@ after it, and FP64 block-sum checks for the read pattern.  Copy traffic is
 2 x buffer bytes; read traffic is buffer bytes + the FP32 sink.
 
 Launch configurations are this build's own: the copy probe sweeps the
-persistent 128-bit kernel over threads per CTA and the bulk-copy-engine
-kernel; the read probe sweeps elements per CTA (--block-sizes) and warps.
+128-bit kernel (one CTA per piece of threads x 32 bytes) over threads per
+CTA, and the bulk-copy-engine kernel over ring depths; the read probe sweeps
+elements per CTA (--block-sizes) and warps.
 """
 
 from __future__ import annotations
@@ -44,20 +45,21 @@ def parse_args(argv=None):
                         help="Elements per CTA of the read pattern (powers of two)")
     parser.add_argument("--num-warps", type=positive_int, nargs="+",
                         help="Warps per CTA of the read pattern (default: 4 8)")
-    parser.add_argument("--copy-threads", type=positive_int, nargs="+", default=[256, 512, 1024],
+    parser.add_argument("--copy-threads", type=positive_int, nargs="+", default=[512, 768, 1024],
                         help="Threads per CTA of the 128-bit copy kernel")
     parser.add_argument("--copy-variants", choices=list(COPY_VARIANTS), nargs="+",
                         default=list(COPY_VARIANTS), help="Copy kernels to measure")
     parser.add_argument("--bulk-stages", type=positive_int, nargs="+", default=[2, 4],
                         help="Shared-memory ring depths (32 KiB chunks) of the bulk-copy kernel")
     parser.add_argument("--copy-blocks-per-sm", type=positive_int, nargs="+", default=[4],
-                        help="CTAs per SM of the copy kernels (grid = value x SMs)")
+                        help="CTAs per SM of the bulk-copy kernel (grid = value x SMs); the "
+                             "128-bit kernel launches one CTA per piece")
     parser.add_argument("--quick", action="store_true",
                         help="Smoke check: 8 MiB, one configuration per mode; not an HBM result")
     args = parser.parse_args(argv)
     if args.quick:
         args.sizes_mib, args.block_sizes, args.num_warps = [8], [1024], None
-        args.copy_threads, args.copy_variants = [512], ["ldg128"]
+        args.copy_threads, args.copy_variants = [768], ["ldg128"]
         args.bulk_stages, args.copy_blocks_per_sm = [4], [4]
     if any(b & (b - 1) or b > 65536 or b < 256 for b in args.block_sizes):
         parser.error("--block-sizes must be powers of two in [256, 65536]")
@@ -72,14 +74,11 @@ def parse_args(argv=None):
 
 def copy_configs(args, sms: int):
     configs = []
-    for per_sm in args.copy_blocks_per_sm:
-        for variant in args.copy_variants:
-            if variant == "ldg128":
-                configs += [{"variant": variant, "threads": t, "blocks": per_sm * sms}
-                            for t in args.copy_threads]
-            else:
-                configs += [{"variant": variant, "stages": st, "threads": 32,
-                             "blocks": per_sm * sms} for st in args.bulk_stages]
+    if "ldg128" in args.copy_variants:
+        configs += [{"variant": "ldg128", "threads": t, "blocks": 0} for t in args.copy_threads]
+    if "bulk" in args.copy_variants:
+        configs += [{"variant": "bulk", "stages": st, "threads": 32, "blocks": per_sm * sms}
+                    for per_sm in args.copy_blocks_per_sm for st in args.bulk_stages]
     return configs
 
 
@@ -169,7 +168,7 @@ def main(argv=None):
                 knob = config["stages"] if config["variant"] == "bulk" else config["threads"]
                 label = (f"bulk/{config['stages']}st/{config['blocks']}b"
                          if config["variant"] == "bulk"
-                         else f"ldg128/{config['threads']}t/{config['blocks']}b")
+                         else f"ldg128/{config['threads']}t/pieces")
                 info = _native.kernel_info(_native.FAMILY_COPY, COPY_VARIANTS[config["variant"]],
                                            knob)
             else:

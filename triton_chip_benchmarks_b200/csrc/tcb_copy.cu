@@ -1,9 +1,22 @@
 // Device copy and read bandwidth probes (sm_100a).
 //
 // copy: dst = src over a byte range.  Two kernels:
-//   * LDG128 - persistent grid-stride loop; each thread keeps UNROLL 16-byte
-//     loads in flight before storing them (streaming load/store hints keep the
-//     one-pass data out of L1 and mark it evict-first in L2).
+//   * LDG128 - register copy, one CTA per piece of THREADS x 32 bytes: each
+//     thread loads its 32 bytes (one 256-bit vector when both pointers are
+//     32-byte aligned, else two 16-byte vectors a CTA width apart, both in
+//     flight) and stores them.  The CTA size is a template parameter for the
+//     common sizes.  An explicit grid size walks the pieces grid-stride
+//     instead (a second kernel).
+//     Measured on B200 (2-4 GiB): 768-thread CTAs, two resident per SM (48 KB
+//     of loads in flight per SM), copy at 7.0-7.1 TB/s; 1024 threads 7.0,
+//     128-512 threads 6.92-6.96, one or three 16-byte vectors per thread
+//     6.16-6.97; the same code inside a grid-stride loop (even one that runs
+//     once) 6.57 at 768 threads, persistent grids of 2-16 CTAs per SM
+//     5.9-6.4.  256-bit vectors hold 7.08-7.11 at every source/destination
+//     offset tried, where two 16-byte vectors dip to 6.96.  Any shared memory
+//     on the CTA costs L1 capacity, which holds the in-flight loads: the same
+//     pieces with 48 KB of shared memory per CTA copy at 6.2 TB/s, which is
+//     also where the bulk-copy ring below (6.6-6.7 TB/s) loses.
 //   * BULK   - the bulk-copy engine: one lane per CTA moves CHUNK-byte pieces
 //     global -> shared -> global through a ring of STAGES buffers; completion
 //     of loads is tracked by mbarriers, of stores by bulk groups.
@@ -23,7 +36,8 @@
 namespace tcb {
 namespace {
 
-constexpr int kCopyUnroll = 4;
+constexpr int kCopyVectors = 2;       // 16-byte vectors per thread of the LDG128 kernel
+constexpr int kCopyDefaultThreads = 768;
 constexpr int kBulkChunk = 32768;
 constexpr int kBulkMaxStages = 8;
 constexpr int kBulkDefaultStages = 2;
@@ -50,21 +64,80 @@ __device__ __forceinline__ void copy_tail(const unsigned char* src, unsigned cha
   }
 }
 
-__global__ void __launch_bounds__(1024)
-    copy_ldg128_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t bytes) {
-  const size_t nvec = bytes >> 4;
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; i + (kCopyUnroll - 1) * stride < nvec; i += kCopyUnroll * stride) {
-    uint4 v[kCopyUnroll];
+struct alignas(32) Vec32 {
+  uint32_t w[8];
+};
+
+__device__ __forceinline__ Vec32 ld_v8(const Vec32* p) {
+  Vec32 v;
+  asm volatile("ld.global.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]),
+                 "=r"(v.w[5]), "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_v8(Vec32* p, const Vec32& v) {
+  asm volatile("st.global.v8.u32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v.w[0]),
+               "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]),
+               "r"(v.w[7])
+               : "memory");
+}
+
+// One piece of THREADS x 32 bytes per CTA over nvec 16-byte vectors.
+// THREADS = 0: the CTA size is blockDim.x.  WIDE: 256-bit vectors (both
+// pointers 32-byte aligned); an odd last 16-byte vector goes to the thread
+// just past the 256-bit ones.
+template <int THREADS, bool WIDE>
+__global__ void __launch_bounds__(THREADS ? THREADS : 1024)
+    copy_piece_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t nvec) {
+  const size_t threads = THREADS ? THREADS : blockDim.x;
+  if constexpr (WIDE) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * threads + threadIdx.x;
+    const size_t n32 = nvec >> 1;
+    if (i < n32)
+      st_v8(reinterpret_cast<Vec32*>(dst) + i, ld_v8(reinterpret_cast<const Vec32*>(src) + i));
+    else if (i == n32 && (nvec & 1))
+      st_stream_v4(dst + nvec - 1, ld_stream_v4(src + nvec - 1));
+  } else {
+    const size_t i = static_cast<size_t>(blockIdx.x) * threads * kCopyVectors + threadIdx.x;
+    uint4 v[kCopyVectors];
 #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) v[u] = ld_stream_v4(src + i + u * stride);
+    for (int u = 0; u < kCopyVectors; ++u)
+      if (i + u * threads < nvec) v[u] = ld_stream_v4(src + i + u * threads);
 #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) st_stream_v4(dst + i + u * stride, v[u]);
+    for (int u = 0; u < kCopyVectors; ++u)
+      if (i + u * threads < nvec) st_stream_v4(dst + i + u * threads, v[u]);
   }
-  for (; i < nvec; i += stride) st_stream_v4(dst + i, ld_stream_v4(src + i));
-  copy_tail(reinterpret_cast<const unsigned char*>(src), reinterpret_cast<unsigned char*>(dst),
-            nvec << 4, bytes);
+}
+
+// The same pieces walked grid-stride by a grid of any size.
+__global__ void __launch_bounds__(1024)
+    copy_stride_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t nvec) {
+  const size_t piece = static_cast<size_t>(blockDim.x) * kCopyVectors;
+  for (size_t p = blockIdx.x; p * piece < nvec; p += gridDim.x) {
+    const size_t i = p * piece + threadIdx.x;
+    uint4 v[kCopyVectors];
+#pragma unroll
+    for (int u = 0; u < kCopyVectors; ++u)
+      if (i + u * blockDim.x < nvec) v[u] = ld_stream_v4(src + i + u * blockDim.x);
+#pragma unroll
+    for (int u = 0; u < kCopyVectors; ++u)
+      if (i + u * blockDim.x < nvec) st_stream_v4(dst + i + u * blockDim.x, v[u]);
+  }
+}
+
+using PieceFn = void (*)(const uint4*, uint4*, size_t);
+
+// The one-shot kernel for a CTA size (compile-time for the common sizes).
+PieceFn copy_piece_fn(int threads, bool wide) {
+  switch (threads) {
+    case 256: return wide ? copy_piece_kernel<256, true> : copy_piece_kernel<256, false>;
+    case 512: return wide ? copy_piece_kernel<512, true> : copy_piece_kernel<512, false>;
+    case 768: return wide ? copy_piece_kernel<768, true> : copy_piece_kernel<768, false>;
+    case 1024: return wide ? copy_piece_kernel<1024, true> : copy_piece_kernel<1024, false>;
+    default: return wide ? copy_piece_kernel<0, true> : copy_piece_kernel<0, false>;
+  }
 }
 
 __global__ void copy_bytes_kernel(const unsigned char* __restrict__ src,
@@ -259,11 +332,28 @@ extern "C" int tcb_copy(const void* src, void* dst, size_t bytes, int variant, i
     return launch_status();
   }
   if (variant == TCB_COPY_LDG128) {
-    if (threads == 0) threads = 512;
+    if (threads == 0) threads = kCopyDefaultThreads;
     if (threads < 32 || threads > 1024 || threads % 32) return TCB_ERR_INVALID_ARGUMENT;
-    if (blocks == 0) blocks = facts.sm_count * (2048 / threads);
-    copy_ldg128_kernel<<<blocks, threads, 0, s>>>(static_cast<const uint4*>(src),
-                                                  static_cast<uint4*>(dst), bytes);
+    const size_t nvec = bytes >> 4;
+    const size_t piece_vecs = static_cast<size_t>(threads) * kCopyVectors;
+    const size_t pieces = (nvec + piece_vecs - 1) / piece_vecs;
+    if (pieces > 0x7fffffffULL) return TCB_ERR_INVALID_ARGUMENT;
+    if (pieces > 0) {
+      const auto* s4 = static_cast<const uint4*>(src);
+      auto* d4 = static_cast<uint4*>(dst);
+      if (blocks > 0 && static_cast<size_t>(blocks) < pieces) {
+        copy_stride_kernel<<<blocks, threads, 0, s>>>(s4, d4, nvec);
+      } else {
+        const bool wide = aligned(src, 32) && aligned(dst, 32);
+        copy_piece_fn(threads, wide)<<<static_cast<unsigned>(pieces), threads, 0, s>>>(s4, d4,
+                                                                                       nvec);
+      }
+    }
+    if (bytes & 15) {
+      const size_t body = nvec << 4;
+      copy_bytes_kernel<<<1, 32, 0, s>>>(static_cast<const unsigned char*>(src) + body,
+                                         static_cast<unsigned char*>(dst) + body, bytes & 15);
+    }
     return launch_status();
   }
   // Bulk-copy engine: one warp per CTA (lane 0 drives the ring); `threads`
@@ -318,18 +408,21 @@ extern "C" int tcb_read(const void* src, int dtype, long long elements, float* s
 namespace tcb {
 int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out) {
   cudaFuncAttributes attr;
-  const void* fn = variant == TCB_COPY_BULK ? reinterpret_cast<const void*>(copy_bulk_kernel)
-                                            : reinterpret_cast<const void*>(copy_ldg128_kernel);
+  const void* fn = variant == TCB_COPY_BULK
+                       ? reinterpret_cast<const void*>(copy_bulk_kernel)
+                       : reinterpret_cast<const void*>(
+                             copy_piece_fn(threads ? threads : kCopyDefaultThreads, true));
   if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
   out->dynamic_smem_bytes =
       variant == TCB_COPY_BULK ? copy_bulk_smem_bytes(copy_bulk_stages(threads)) : 0;
-  out->threads_per_block = variant == TCB_COPY_BULK ? 32 : (threads ? threads : 512);
+  out->threads_per_block = variant == TCB_COPY_BULK ? 32 : (threads ? threads : kCopyDefaultThreads);
   out->tensor_core = 0;
   copy_str(out->instruction, sizeof(out->instruction),
            variant == TCB_COPY_BULK
                ? "cp.async.bulk.shared::cluster.global / cp.async.bulk.global.shared::cta"
-               : "ld.global.nc.L1::no_allocate.v4.u32 / st.global.cs.v4.u32");
+               : "ld.global.v8.u32 / st.global.v8.u32 (32-byte aligned; else "
+                 "ld.global.nc.v4.u32 / st.global.cs.v4.u32)");
   copy_str(out->execution_kind, sizeof(out->execution_kind), "memory");
   return TCB_OK;
 }

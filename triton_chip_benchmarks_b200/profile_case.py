@@ -154,7 +154,7 @@ def main(argv=None):
     sub = parser.add_subparsers(dest="case", required=True)
     p = sub.add_parser("copy")
     p.add_argument("--mib", type=int, default=1024)
-    p.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
+    p.add_argument("--variant", choices=("ldg128", "bulk"), default="ldg128")
     p.add_argument("--threads", type=int, default=0)
     p.add_argument("--blocks", type=int, default=0)
     p.add_argument("--launches", type=int, default=3)

@@ -40,7 +40,7 @@ def build_parser():
     parser.add_argument("--output", type=Path)
     # probe configuration
     parser.add_argument("--mib", type=int, default=4096, help="copy: bytes per buffer in MiB")
-    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="bulk")
+    parser.add_argument("--variant", choices=("ldg128", "bulk"), default="ldg128")
     parser.add_argument("--dtype", default="bf16")
     parser.add_argument("--kernel", choices=("tcgen05", "dmma", "simt", "simt_reg"),
                         default="tcgen05")
