@@ -9,12 +9,16 @@ same GPU.
 
     python baseline/triton_suite.py --install /path/to/reference   # once, here
     python baseline/triton_suite.py --output out/triton_suite.json [suite flags]
+    python baseline/triton_suite.py --child bench_vector --output out/v.json --dtype bf16 ...
 
 ``--install`` copies the reference's top-level Python modules into
 ``baseline/_ref`` (git-ignored; it travels with the working tree to the GPU
 box).  Every other flag goes to the reference's ``bench_suite.py`` unchanged
 (``--device``, ``--timing``, ``--quick``, ``--metrics``, ``--timeout`` ...).
 With ``--compare OURS.json`` the two tables are printed side by side.
+``--child NAME`` runs one of the reference's per-metric scripts (``NAME.py``:
+bench_bandwidth, bench_tensor, bench_vector) the same way, for a single row
+(the reference's suite runner has no metric filter).
 """
 
 from __future__ import annotations
@@ -41,14 +45,15 @@ def install(source: Path) -> None:
     print(f"copied {len(modules)} modules into {REF}")
 
 
-def run(suite_args: list[str], output: Path) -> int:
-    if not (REF / "bench_suite.py").exists():
-        raise SystemExit(f"{REF} is empty; run with --install <reference checkout> first")
+def run(suite_args: list[str], output: Path, script: str = "bench_suite") -> int:
+    if not (REF / f"{script}.py").exists():
+        raise SystemExit(f"{REF / (script + '.py')} is missing; run with --install <reference "
+                         "checkout> first")
     env = dict(os.environ)
     env["PYTHONPATH"] = os.pathsep.join(
         [str(HERE), str(REF)] + ([env["PYTHONPATH"]] if env.get("PYTHONPATH") else []))
     output.parent.mkdir(parents=True, exist_ok=True)
-    command = [sys.executable, "-u", str(REF / "bench_suite.py"), "--output", str(output),
+    command = [sys.executable, "-u", str(REF / f"{script}.py"), "--output", str(output),
                *suite_args]
     print("running:", " ".join(command), flush=True)
     return subprocess.run(command, env=env, check=False).returncode
@@ -78,12 +83,14 @@ def main() -> int:
     parser.add_argument("--output", type=Path, default=Path("gpurun_out/triton_suite.json"))
     parser.add_argument("--compare", type=Path, metavar="OURS",
                         help="print this repository's table JSON beside the reference's")
+    parser.add_argument("--child", choices=("bench_bandwidth", "bench_tensor", "bench_vector"),
+                        help="run one per-metric script of the reference instead of its suite")
     args, suite_args = parser.parse_known_args()
     if args.install is not None:
         install(args.install)
         return 0
-    rc = run(suite_args, args.output)
-    if args.compare is not None and args.output.exists():
+    rc = run(suite_args, args.output, args.child or "bench_suite")
+    if args.child is None and args.compare is not None and args.output.exists():
         compare(args.output, args.compare)
     return rc
 
