@@ -121,10 +121,12 @@ int tcb_vector_chains(int dtype, const void *in, void *out, const void *coeff,
 
 /* The same chains with the 9 coefficients read from HOST memory during the
  * call (same storage type and order as `coeff` above) and passed to the kernel
- * by value, where the FMAs can take them as constant-bank operands (FP64
- * chains: 37.0 vs 34.1 TFLOP/s with register-resident coefficients).  The
- * reference-side binding copies its device coefficient tensor to the host once,
- * outside timing. */
+ * by value, where the FMAs can take them as constant-bank operands.  Measured
+ * on B200: FP32 and FP64 chains are faster this way (FP64 37.0 vs 34.1 TFLOP/s
+ * with register-resident coefficients), packed bf16x2/f16x2 and DP4A chains
+ * slower (bf16x2 73.4-74.0 vs 74.1-74.3 TFLOP/s; DP4A 148.2 vs 148.5 TOP/s),
+ * so callers pick the entry point per dtype.  The reference-side binding
+ * copies its device coefficient tensor to the host once, outside timing. */
 int tcb_vector_chains_imm(int dtype, const void *in, void *out, const void *coeff_host,
                           long long elements, int iterations, int blocks, int threads,
                           int elems_per_thread, int unroll, tcb_stream_t stream);
@@ -257,7 +259,9 @@ typedef struct tcb_kernel_info_t {
  * `a0..a5` are the family's launch parameters:
  *   COPY   : variant, threads
  *   READ   : dtype, threads
- *   VECTOR : dtype, threads, elems_per_thread, unroll
+ *   VECTOR : dtype, threads, elems_per_thread, unroll, coefficients (0: passed by
+ *            value, tcb_vector_chains_imm; 1: from device memory into registers,
+ *            tcb_vector_chains)
  *   TENSOR : dtype, variant, tile_m, tile_n, tile_k, chains (blocks_per_sm via a6)
  *   GEMM_FP4 (any GEMM dtype): dtype, M, N (M, N = 0: a large problem); the
  *            kernel tcb_gemm would run for that shape on the current device

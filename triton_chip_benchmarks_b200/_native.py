@@ -30,6 +30,11 @@ COPY_LDG128, COPY_BULK = 0, 1
 READ_FP32, READ_FP16, READ_BF16 = 0, 1, 2
 
 V_BF16, V_FP16, V_FP32, V_FP64, V_INT8_DP4A, V_INT32_IMAD, V_INT8_MULADD = range(7)
+# Where the chains read their coefficients (measured on B200): packed bf16x2/f16x2
+# FMAs and DP4A run fastest with them in registers (tcb_vector_chains, device
+# memory), the other ops with them passed by value as constant-bank operands
+# (tcb_vector_chains_imm).
+COEFF_IN_REGISTERS = frozenset({V_BF16, V_FP16, V_INT8_DP4A})
 
 T_BF16, T_FP16, T_TF32, T_FP32, T_FP64, T_INT8, T_FP8E4M3, T_MXF4 = range(8)
 TV_TCGEN05, TV_DMMA, TV_SIMT, TV_SIMT_REG = 0, 1, 2, 3
@@ -239,6 +244,12 @@ def vector_chains(dtype: int, inputs, outputs, coefficients, elements: int, iter
         else coefficients.ctypes.data
     check(fn(dtype, _ptr(inputs), _ptr(outputs), host_ptr, elements, iterations, blocks, threads,
              elems_per_thread, unroll, _stream(stream)), name)
+
+
+def vector_coefficients(dtype: int, on_device, on_host):
+    """The coefficient tensor to pass to vector_chains for this op: the device
+    copy for the ops that run fastest from registers, else the host copy."""
+    return on_device if dtype in COEFF_IN_REGISTERS else on_host
 
 
 def tensor_peak(dtype: int, variant: int, a, b, c, *, blocks: int, blocks_per_sm: int,

@@ -190,11 +190,11 @@ def vector_row(key: str, device: torch.device, sms: int, warmup: int, window_ms:
     elements = blocks * threads * ept
     args = SimpleNamespace(dtype=key, inputs="baseline", int8_op="imad", seed=seed)
     inputs, coeff = bench_vector.make_inputs(args, elements, device)
-    coeff_host = coeff.cpu().contiguous()
+    coeff_arg = _native.vector_coefficients(code, coeff, coeff.cpu().contiguous())
     output = torch.empty_like(inputs)
 
     def run():
-        _native.vector_chains(code, inputs, output, coeff_host, elements, VECTOR_ITERATIONS,
+        _native.vector_chains(code, inputs, output, coeff_arg, elements, VECTOR_ITERATIONS,
                               blocks, threads, ept, unroll)
 
     run()
@@ -204,6 +204,7 @@ def vector_row(key: str, device: torch.device, sms: int, warmup: int, window_ms:
     ops = 2 * 8 * elements * VECTOR_ITERATIONS
     config = {"blocks": blocks, "threads": threads, "elements_per_thread": ept,
               "accumulator_registers_per_thread": 8, "unroll": unroll,
+              "coefficients": "registers" if code in _native.COEFF_IN_REGISTERS else "by value",
               "iterations": VECTOR_ITERATIONS,
               "operation": "int32 x*1+1 (wrap)" if key == "int8" else "x*a+b, a=1-2^-10, b=2^-10"}
     return _row(f"vector_{key}", ops, timing, config, validation, sms, peaks)

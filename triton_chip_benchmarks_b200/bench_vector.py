@@ -215,16 +215,18 @@ def run_benchmark(args, metadata):
                         continue
                     per_thread = block_size // threads
                     info = _native.kernel_info(_native.FAMILY_VECTOR, ndtype, threads, per_thread,
-                                               unroll)
+                                               unroll, int(ndtype in _native.COEFF_IN_REGISTERS))
                     if info["local_bytes_per_thread"]:
                         exclude("register_spills", f"local={info['local_bytes_per_thread']} B",
                                 **config)
                         continue
 
+                    coeff_arg = _native.vector_coefficients(ndtype, coeff, coeff_host)
+
                     def run(iterations=args.iterations, unroll_value=unroll,
                             per_thread=per_thread, threads=threads):
-                        # Host coefficients: passed to the kernel by value.
-                        _native.vector_chains(ndtype, inputs, output, coeff_host, elements,
+                        # Coefficients in registers or by value, per op.
+                        _native.vector_chains(ndtype, inputs, output, coeff_arg, elements,
                                               iterations, blocks, threads, per_thread,
                                               unroll_value)
 
@@ -281,7 +283,10 @@ def run_benchmark(args, metadata):
                         if is_int else args.dtype,
                         "includes_unpacking": False,
                         "operation": operation, "input_pattern": args.inputs,
-                        "loop_structure": "strip_mined", "coefficient_load": "kernel_parameter",
+                        "loop_structure": "strip_mined",
+                        "coefficient_load": ("device_memory_to_registers"
+                                             if ndtype in _native.COEFF_IN_REGISTERS
+                                             else "kernel_parameter"),
                         "hardware_fusion_verified": not is_int,
                         "explicit_fma_supported": not is_int,
                         "dp4a_used": is_int and args.int8_op == "dp4a",

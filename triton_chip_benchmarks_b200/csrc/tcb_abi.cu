@@ -115,7 +115,7 @@ extern "C" int tcb_kernel_info(int family, int a0, int a1, int a2, int a3, int a
     case TCB_FAMILY_READ:
       return read_kernel_info(a0, a1, out);
     case TCB_FAMILY_VECTOR:
-      return vector_kernel_info(a0, a1, a2, a3, out);
+      return vector_kernel_info(a0, a1, a2, a3, a4, out);
     case TCB_FAMILY_TENSOR:
       return tensor_kernel_info(a0, a1, a2, a3, a4, a5, a6, out);
     case TCB_FAMILY_GEMM_FP4:

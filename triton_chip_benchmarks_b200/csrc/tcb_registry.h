@@ -19,7 +19,7 @@ inline void fill_kernel_info(const cudaFuncAttributes& attr, tcb_kernel_info_t* 
 int copy_kernel_info(int variant, int threads, tcb_kernel_info_t* out);
 int read_kernel_info(int dtype, int threads, tcb_kernel_info_t* out);
 int vector_kernel_info(int dtype, int threads, int elems_per_thread, int unroll,
-                       tcb_kernel_info_t* out);
+                       int coeff_in_registers, tcb_kernel_info_t* out);
 int gemm_kernel_info(int dtype, int m, int n, tcb_kernel_info_t* out);
 int gemm_cuda_core_info(int dtype, tcb_kernel_info_t* out);
 int gemm_cuda_core(int dtype, const void* A, const void* B, void* C, int M, int N, int K,

@@ -286,7 +286,9 @@ template <typename Op>
 int launch_op(int e, int u, const void* in, void* out, const void* coeff, const void* imm_host,
               long long words, int iterations, int blocks, int threads, cudaStream_t s,
               bool query_only, const void** fn_out) {
-  ChainFnT<Op> fn = imm_host != nullptr || query_only ? pick<Op, true>(e, u) : pick<Op, false>(e, u);
+  // A query asks for the by-value variant with a non-null imm_host and for
+  // the register variant with a non-null coeff (neither is dereferenced).
+  ChainFnT<Op> fn = imm_host != nullptr ? pick<Op, true>(e, u) : pick<Op, false>(e, u);
   if (fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
   if (fn_out != nullptr) *fn_out = reinterpret_cast<const void*>(fn);
   if (query_only) return TCB_OK;
@@ -330,11 +332,14 @@ int dispatch(int dtype, int e, int u, const void* in, void* out, const void* coe
 }  // namespace
 
 int vector_kernel_info(int dtype, int threads, int elems_per_thread, int unroll,
-                       tcb_kernel_info_t* out) {
+                       int coeff_in_registers, tcb_kernel_info_t* out) {
   OpFacts facts;
   const void* fn = nullptr;
-  int rc = dispatch(dtype, elems_per_thread, unroll, nullptr, nullptr, nullptr, nullptr, 0, 0, 0,
-                    0, nullptr, true, &fn, &facts, false);
+  static const int marker = 0;  // selects the variant; never read
+  const void* by_value = coeff_in_registers ? nullptr : &marker;
+  const void* on_device = coeff_in_registers ? &marker : nullptr;
+  int rc = dispatch(dtype, elems_per_thread, unroll, nullptr, nullptr, on_device, by_value, 0, 0,
+                    0, 0, nullptr, true, &fn, &facts, false);
   if (rc != TCB_OK || fn == nullptr) return TCB_ERR_INVALID_ARGUMENT;
   cudaFuncAttributes attr;
   if (cudaFuncGetAttributes(&attr, fn) != cudaSuccess) return TCB_ERR_DEVICE;

@@ -76,8 +76,10 @@ def launch_read(src, sink, block_size, num_warps, vendor_name):
 # bench_vector.launch_vector(...), bench_vector.py:1032-1051: grid=(blocks,), BLOCK_SIZE
 # elements per program.
 # The reference passes every argument positionally (bench_vector.py:1411-1416); the
-# options after use_dp4a are off on NVIDIA.  The coefficients go to the kernel by
-# value (tcb_vector_chains_imm), from a host copy made once per coefficient tensor.
+# options after use_dp4a are off on NVIDIA.  Packed bf16/fp16 and DP4A chains read
+# the coefficients from device memory into registers (tcb_vector_chains); the others
+# take them by value (tcb_vector_chains_imm), from a host copy made once per
+# coefficient tensor.  (Measured on B200: each op's faster form.)
 # The 16-bit kernels work on packed pairs, so a block of one element per thread runs
 # as half the threads with two elements each (the same elements and iterations).
 
@@ -89,6 +91,11 @@ def launch_vector(kernel, grid, inputs, output, coefficients, elements, iteratio
     threads = (num_warps or 4) * 32
     if dtype in (0, 1) and block_size < 2 * threads:
         threads = block_size // 2
+    if dtype in (0, 1, 4):
+        _check(_lib.tcb_vector_chains(dtype, inputs.data_ptr(), output.data_ptr(),
+                                      coefficients.data_ptr(), elements, iterations, grid[0],
+                                      threads, block_size // threads, unroll, _stream()))
+        return
     host = _once(coefficients, lambda t: t.cpu().contiguous())
     _check(_lib.tcb_vector_chains_imm(dtype, inputs.data_ptr(), output.data_ptr(),
                                       host.data_ptr(), elements, iterations, grid[0],
