@@ -16,6 +16,8 @@ same GPU.
 box).  Every other flag goes to the reference's ``bench_suite.py`` unchanged
 (``--device``, ``--timing``, ``--quick``, ``--metrics``, ``--timeout`` ...).
 With ``--compare OURS.json`` the two tables are printed side by side.
+``--summary IN OUT`` writes a compact copy of a suite JSON (rows without
+command lines or file paths) for the repository's results.
 ``--child NAME`` runs one of the reference's per-metric scripts (``NAME.py``:
 bench_bandwidth, bench_tensor, bench_vector) the same way, for a single row
 (the reference's suite runner has no metric filter).
@@ -59,6 +61,28 @@ def run(suite_args: list[str], output: Path, script: str = "bench_suite") -> int
     return subprocess.run(command, env=env, check=False).returncode
 
 
+ROW_KEYS = ("metric", "group", "precision", "unit", "status", "value", "median_value",
+            "timing_method", "configuration", "reason", "successful_configurations")
+
+
+def summary(source: Path, out: Path) -> None:
+    doc = json.loads(source.read_text())
+    rows = []
+    for row in doc["results"]:
+        kept = {k: row[k] for k in ROW_KEYS if k in row}
+        if "patterns" in row:
+            kept["patterns"] = {name: {k: v for k, v in pattern.items()
+                                       if k in ("value", "median_value", "configuration")}
+                                for name, pattern in row["patterns"].items()}
+        rows.append(kept)
+    device = {k: v for k, v in doc.get("device", {}).items()
+              if k in ("device_name", "architecture", "sm_count", "memory_capacity_gib")}
+    out.write_text(json.dumps({"benchmark": doc.get("benchmark"), "status": doc.get("status"),
+                               "timestamp_utc": doc.get("timestamp_utc"), "device": device,
+                               "measurement_policy": doc.get("measurement_policy"),
+                               "results": rows}, indent=1) + "\n")
+
+
 def compare(reference: Path, ours: Path) -> None:
     theirs = {r["metric"]: r for r in json.loads(reference.read_text())["results"]}
     mine = {r["metric"]: r for r in json.loads(ours.read_text())["results"]}
@@ -83,11 +107,16 @@ def main() -> int:
     parser.add_argument("--output", type=Path, default=Path("gpurun_out/triton_suite.json"))
     parser.add_argument("--compare", type=Path, metavar="OURS",
                         help="print this repository's table JSON beside the reference's")
+    parser.add_argument("--summary", type=Path, nargs=2, metavar=("SUITE_JSON", "OUT"),
+                        help="write a compact copy of a suite JSON and exit")
     parser.add_argument("--child", choices=("bench_bandwidth", "bench_tensor", "bench_vector"),
                         help="run one per-metric script of the reference instead of its suite")
     args, suite_args = parser.parse_known_args()
     if args.install is not None:
         install(args.install)
+        return 0
+    if args.summary is not None:
+        summary(*args.summary)
         return 0
     rc = run(suite_args, args.output, args.child or "bench_suite")
     if args.child is None and args.compare is not None and args.output.exists():

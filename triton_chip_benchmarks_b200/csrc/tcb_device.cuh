@@ -197,24 +197,6 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// tcgen05.cp of a 32-row x 16-byte matrix in shared memory (row r at byte
-// 16 r from the descriptor's start; no swizzle) into four 32-bit columns of
-// tensor memory at `taddr` (lane field 0), the same rows in each 32-lane
-// quarter: row r goes to lane r of every quarter, its bytes 4c..4c+3 to
-// column c.  Issued by one thread; it runs on the tensor pipe in issue order
-// with the tcgen05.mma instructions of the same thread.
-__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
-               : "memory");
-}
-
-// The same for a CTA pair, issued by the leader: each CTA's shared memory at
-// the descriptor's address goes to its own tensor memory at `taddr`.
-__device__ __forceinline__ void tmem_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
-               : "memory");
-}
-
 // ------------------------------------------------------ CTA pairs (cluster of 2)
 // Rank of this CTA in its cluster (0 leads a CTA pair).
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -11,16 +11,19 @@
 //   warp 0      TMA producer: per 128-byte K block, A [128 x 128 B] and
 //               B [256 x 128 B] tiles (SWIZZLE_128B) into a ring of STAGES
 //               shared-memory stages, completing on loaded[stage];
-//   warp 1      MMA issuer: waits loaded[stage], issues the block's four
+//   warp 1      MMA issuer: waits loaded[stage] (and full[stage] for MX
+//               scales), issues the block's four
 //               tcgen05.mma (M=128, N=256, K=32 B each) into one tensor-memory
 //               accumulator, commits to empty[stage]; after the last block
 //               commits to acc_full;
 //   warps 2-5   epilogue: wait acc_full, tcgen05.ld their 32 lanes x 256
-//               columns, store C, arrive acc_empty.
-// MX FP4: the producer also brings each block's packed E8M0 scales into the
-// stage (bulk copies), and the MMA issuer copies them into the stage's
-// tensor-memory scale slot (tcgen05.cp) just before the block's MMAs, which
-// run after the copies in issue order.
+//               columns, store C, arrive acc_empty;
+//   warps 6-9   (MX FP4 only) scale writers: the producer also brings each
+//               block's packed E8M0 scales into the stage (bulk copies); the
+//               scale warps move them from shared memory into a tensor-memory
+//               scale ring slot (same stage index) and arrive on full[stage].
+//               (Copying them with tcgen05.cp from the MMA thread instead ran
+//               3-15 % slower at M <= 128: the copies take tensor-pipe time.)
 // Tiles are visited in groups of 8 row-blocks so concurrent tiles share
 // operands in L2; C is written with streaming (evict-first) stores.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so all roles
@@ -112,10 +115,8 @@ __device__ __forceinline__ void gemm_mma(uint32_t d, uint64_t adesc, uint64_t bd
   }
 }
 
-constexpr int kGemmThreads = (2 + kEpilogueWarps) * 32;
-
 template <int KIND, int HALVES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__((6 + kScaleWarps) * 32, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                 const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_c, const GemmArgs args) {
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int kTileM = T::kM;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t loaded[kMaxStages];  // TMA bytes of the stage landed
+  __shared__ __align__(8) uint64_t full[kMaxStages];    // MX scales written to tensor memory
   __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ __align__(8) uint64_t acc_full;
   __shared__ __align__(8) uint64_t acc_empty;
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (args.tma_store) prefetch_tensormap(&map_c);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&loaded[s], 1);
+      mbar_init(&full[s], kScaleWarps);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full, 1);
@@ -204,15 +207,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int s = it % kStages;
           const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
           if (!wait_or_abort(&loaded[s], phase, &abort_flag, args.status)) break;
+          if constexpr (kScaled) {
+            if (!wait_or_abort(&full[s], phase, &abort_flag, args.status)) break;
+          }
           tc_fence_after();
           const uint32_t a_lo = smem0 + static_cast<uint32_t>(s * kStageBytes >> 4);
           const uint32_t b_lo = a_lo + (kStageA >> 4);
           const uint32_t sf = tbase + kAccCols + static_cast<uint32_t>(s * kSfStageCols);
-          if constexpr (kScaled) {
-            // The stage's scales (A, B rows 0-127, B rows 128-255; 1 KB each).
-            const uint32_t ss = b_lo + (T::kStageB >> 4);
-            copy_scale_block<false>(sf, ss, ss + 64, ss + 128);
-          }
 #pragma unroll
           for (int k = 0; k < kStepsPerBlock; ++k) {
             const uint64_t bd = desc_const | (b_lo + static_cast<uint32_t>(k * 2));
@@ -270,6 +271,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group_all();  // C stores complete before the CTA retires
+  } else if (kScaled) {
+    // ------------------------------------------------------ scale writers
+    // The producer brings each block's packed scales into the stage with the
+    // operands; lane l takes rows 32j+l (8 bytes each) from shared memory and
+    // writes them into the tensor-memory scale ring slot of the same stage.
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tbase + ((32u * quarter) << 16) + kAccCols;
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+      for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t phase = static_cast<uint32_t>(it / kStages) & 1u;
+        if (!wait_or_abort(&loaded[s], phase, &abort_flag, args.status)) break;
+        const uint8_t* ss = smem + s * kStageBytes + kStageA + T::kStageB + lane * 16;
+        write_scale_block(lane_base + static_cast<uint32_t>(s * kSfStageCols), ss, ss + 1024,
+                          ss + 2048);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+    }
   }
 
   tc_fence_before();
@@ -431,7 +454,7 @@ int gemm_kernel_info(int dtype, int m, int n, tcb_kernel_info_t* out) {
     return TCB_ERR_DEVICE;
   fill_kernel_info(attr, out);
   out->dynamic_smem_bytes = gemm_smem(kind, halves);
-  out->threads_per_block = kGemmThreads;
+  out->threads_per_block = (6 + kScaleWarps) * 32;
   out->tensor_core = 1;
   out->pipeline_stages = gemm_stages(kind, halves);
   out->tile_m = 128 * halves;
@@ -450,9 +473,10 @@ int gemm_kernel_info(int dtype, int m, int n, tcb_kernel_info_t* out) {
 // 96+l, in that order.
 //   dst[((r/128) * (groups_p/8) + g/8) * 1024 + (g%8/4) * 512 + (r%32) * 16
 //       + (r%128/32) * 4 + g%4] = src[r][g].
-// A half is the 32-row x 16-byte source of one tcgen05.cp.32x128b.warpx4 that
-// fills the tensor-memory scale words of two MMA K steps.  Threads walk dst
-// in order, so the stores are coalesced.
+// A scale-writer lane reads its 16 bytes of a half with one load, and they are
+// exactly its tensor-memory words for two MMA K steps; a half is also the
+// 32-row x 16-byte source format of tcgen05.cp.32x128b.warpx4.  Threads walk
+// dst in order, so the stores are coalesced.
 __global__ void mx_scales_pack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                       int rows, int groups, long long total, int group_blocks) {
   for (long long o = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < total;
@@ -553,7 +577,7 @@ extern "C" int tcb_gemm(int dtype, const void* A, const void* B, const void* SA,
   if (blocks == 0) blocks = facts.sm_count;
   if (blocks > tiles) blocks = tiles;
   clear_stale_error();
-  fn<<<blocks, kGemmThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  fn<<<blocks, (6 + kScaleWarps) * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       map_a, map_b, map_c, args);
   return launch_status();
 }

@@ -37,35 +37,29 @@ __device__ __forceinline__ uint32_t sf_idesc(uint32_t idesc, int k) {
   return idesc | (id << 29) | (id << 4);  // A scale factor ID [29,31), B [4,6)
 }
 
-// Scales of one K block into the tensor-memory slot at column `sf`, by
-// tcgen05.cp from shared memory.  `sa`, `sb0` and `sb1` are the 1 KB packed
-// blocks (tcb_mx_scales_pack layout) of A's 128 rows and of B rows 0-127 and
-// 128-255, as shared-memory addresses in 16-byte units.  Half kp (512 bytes)
-// of a block is the 32 x 16-byte copy source for the word of K steps 2kp and
-// 2kp+1: lane l's 16 bytes hold the four scales of rows l, 32+l, 64+l and
-// 96+l, so column j of the copy holds rows 32j+l, the layout that sf_cols_a
-// and sf_cols_b address.  PAIR: issued by a pair's leader (cta_group::2).
-template <bool PAIR>
-__device__ __forceinline__ void copy_scale_block(uint32_t sf, uint32_t sa, uint32_t sb0,
-                                                 uint32_t sb1) {
-  const uint64_t d = smem_desc(0, 128, 128, 0);
+// Scales of one K block into this warp's lane quarter of the tensor-memory
+// slot at `lane_col` (tcgen05.st, two K steps per 32-bit word).  `a`, `b0` and
+// `b1` point at this lane's 16 bytes (lane x 16) of the 1 KB packed blocks
+// (tcb_mx_scales_pack layout) of A's 128 rows and of B rows 0-127 and
+// 128-255 in shared memory.  In each 512-byte half (K steps 2kp, 2kp+1) those
+// 16 bytes are the lane's words for rows l, 32+l, 64+l, 96+l: A's four
+// columns, and B's eight with the second block.
+__device__ __forceinline__ void write_scale_block(uint32_t lane_col, const uint8_t* a,
+                                                  const uint8_t* b0, const uint8_t* b1) {
 #pragma unroll
   for (int kp = 0; kp < 2; ++kp) {
-    const uint32_t col = sf + static_cast<uint32_t>(kp * kSfPairCols);
-    const uint32_t half = static_cast<uint32_t>(kp * (512 >> 4));
-    if constexpr (PAIR) {
-      tmem_cp_32x128b_x4_pair(col, d | (sa + half));
-      tmem_cp_32x128b_x4_pair(col + 4, d | (sb0 + half));
-      tmem_cp_32x128b_x4_pair(col + 8, d | (sb1 + half));
-    } else {
-      tmem_cp_32x128b_x4(col, d | (sa + half));
-      tmem_cp_32x128b_x4(col + 4, d | (sb0 + half));
-      tmem_cp_32x128b_x4(col + 8, d | (sb1 + half));
-    }
+    const uint4 wa = *reinterpret_cast<const uint4*>(a + kp * 512);
+    const uint4 w0 = *reinterpret_cast<const uint4*>(b0 + kp * 512);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(b1 + kp * 512);
+    const uint32_t va[4] = {wa.x, wa.y, wa.z, wa.w};
+    const uint32_t vb[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    tmem_st_4cols(lane_col + static_cast<uint32_t>(kp * kSfPairCols), va);
+    tmem_st_8cols(lane_col + static_cast<uint32_t>(kp * kSfPairCols) + 4, vb);
   }
 }
 constexpr int kTmemCols = 512;
 constexpr int kEpilogueWarps = 4;
+constexpr int kScaleWarps = 4;
 
 struct GemmArgs {
   const uint8_t* sa;  // [M][K/32] E8M0 (MX FP4)

@@ -34,7 +34,9 @@
 // epilogue warps that each load their whole 32 x 64 slice into registers and
 // release it at once, so the next tile's MMAs start while C is written.  C
 // leaves through shared memory and TMA tensor stores: two 4 KB staging
-// buffers, each taken in a fixed turn order by the 8 warps of one group.
+// buffers, each taken in a fixed turn order by the 8 warps of one group; on a
+// pair's last tile, when the operand ring is idle, each warp stages its slice
+// in the ring and stores it without turns.
 // Direct stores of these rows (32 rows x 16 bytes per instruction, or shuffle-
 // transposed to whole lines) slowed the scale writers and the MMA issue; TMA
 // stores did not.
@@ -108,6 +110,8 @@ static_assert(kPairSmem <= 227 * 1024 - 256, "shared memory overflow");
 static_assert(kPairSlotOffset % 1024 == 0 && kPairStagingOffset % 1024 == 0,
               "operand stages and staging buffers keep the 1024-byte swizzle alignment");
 static_assert(kPairEpiCols == 64, "an epilogue warp drains two 32-column loads");
+static_assert(kPairEpiWarps * 2 * kEpiChunkBytes <= kPairStages * kPairStageBytes,
+              "the last tile's C slices fit in the operand ring");
 
 struct PairArgs {
   const uint8_t* sa;  // packed E8M0 scales of A (tcb_mx_scales_pack layout)
@@ -364,7 +368,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tile_coords(pair + ti * pairs, args.tiles_m, args.tiles_n, &tm, &tn);
       const int row0 = tm * 2 * kPairRows + static_cast<int>(rank) * kPairRows + 32 * quarter;
       const int c = tn * kTileN + col0;
-      if (args.tma_store) {
+      if (args.tma_store && ti + 1 == my_tiles) {
+        // Last tile: every MMA has finished reading the operand ring (acc_full
+        // follows their completion) and no load refills it, so each warp
+        // stages its whole slice in 8 KB of the ring of its own and stores it
+        // at once instead of waiting for staging turns (with one or two tiles
+        // per pair the turns were the critical path).
+        uint8_t* own = smem + (warp - 2) * 2 * kEpiChunkBytes;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) stage_chunk(own + q * kEpiChunkBytes, lane, r[q]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+            tma_store_2d(&map_c, c + 32 * q, row0, own + q * kEpiChunkBytes);
+          bulk_commit_group();
+        }
+        __syncwarp();
+      } else if (args.tma_store) {
         const int mine = ti * kPairEpiGroupWarps + slot;
         if (!__all_sync(0xffffffffu, turn_wait(mine))) break;
         __threadfence_block();
@@ -410,19 +432,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
       for (int q = 0; q < kPairPanels; ++q) {
         if (q >= nkb) break;
-#pragma unroll
-        for (int kp = 0; kp < 2; ++kp) {
-          const uint8_t* h = ss + q * 1024 + kp * 512;
-          const uint4 a = *reinterpret_cast<const uint4*>(h);
-          const uint4 b0 = *reinterpret_cast<const uint4*>(h + kPairPanels * 1024);
-          const uint4 b1 = *reinterpret_cast<const uint4*>(h + 2 * kPairPanels * 1024);
-          const uint32_t va[4] = {a.x, a.y, a.z, a.w};
-          const uint32_t vb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-          const uint32_t col = lane_base + static_cast<uint32_t>(slot * kPairSfCols +
-                                                                 q * kSfStageCols + kp * kSfPairCols);
-          tmem_st_4cols(col, va);
-          tmem_st_8cols(col + 4, vb);
-        }
+        const uint8_t* h = ss + q * 1024;
+        write_scale_block(lane_base + static_cast<uint32_t>(slot * kPairSfCols + q * kSfStageCols),
+                          h, h + kPairPanels * 1024, h + 2 * kPairPanels * 1024);
       }
       tmem_wait_st();
       tc_fence_before();
