@@ -44,7 +44,7 @@ def parse_args(argv=None):
     parser.add_argument("--block-sizes", type=positive_int, nargs="+", default=[1024, 4096, 16384],
                         help="Elements per CTA of the read pattern (powers of two)")
     parser.add_argument("--num-warps", type=positive_int, nargs="+",
-                        help="Warps per CTA of the read pattern (default: 4 8)")
+                        help="Warps per CTA of the read pattern (default: 4 8 16 32)")
     parser.add_argument("--copy-threads", type=positive_int, nargs="+", default=[512, 768, 1024],
                         help="Threads per CTA of the 128-bit copy kernel")
     parser.add_argument("--copy-variants", choices=list(COPY_VARIANTS), nargs="+",
@@ -64,7 +64,7 @@ def parse_args(argv=None):
     if any(b & (b - 1) or b > 65536 or b < 256 for b in args.block_sizes):
         parser.error("--block-sizes must be powers of two in [256, 65536]")
     if args.num_warps is None:
-        args.num_warps = [4] if args.quick else [4, 8]
+        args.num_warps = [4] if args.quick else [4, 8, 16, 32]
     if any(w not in (4, 8, 16, 32) for w in args.num_warps):
         parser.error("--num-warps must be 4, 8, 16 or 32")
     if any(t % 32 or t > 1024 for t in args.copy_threads):
