@@ -50,14 +50,15 @@
 //                (waiting empty, completing on the LEADER's loaded, which
 //                expects the bytes of both CTAs);
 //   warp 1       (leader only) MMA issuer: waits acc_empty, loaded and full,
-//                issues four pair MMAs per K block, commits empty and sempty
+//                issues four pair MMAs per K block, commits empty and tfree
 //                to both CTAs, and acc_full to both CTAs after each tile;
 //   warps 2-17   epilogue (see above), arriving on the leader's acc_empty;
-//   warps 18-21  scale writers: move this CTA's staged scales into their
-//                tensor-memory slot (warp w writes lane quarter w % 4) and
-//                arrive on the leader's full;
+//   warps 18-21  scale writers: wait sloaded and tfree, move this CTA's
+//                staged scales into their tensor-memory slot (warp w writes
+//                lane quarter w % 4), arrive on this CTA's sfree and the
+//                leader's full;
 //   warp 22      scale loader: bulk-copies each stage's scales into its slot
-//                (waiting sempty, completing on this CTA's sloaded).
+//                (waiting sfree, completing on this CTA's sloaded).
 // Every wait is bounded; a wait that fails raises the abort flag of both
 // CTAs, so the pair leaves its loops together.  A cluster barrier follows
 // barrier set-up and precedes teardown, so neither CTA exits while its peer
@@ -176,8 +177,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   __shared__ __align__(8) uint64_t loaded[kPairStages];   // leader: both operand halves landed
   __shared__ __align__(8) uint64_t empty[kPairStages];    // pair MMAs done with the stage
   __shared__ __align__(8) uint64_t sloaded[kPairSlots];   // this CTA's scales landed
+  __shared__ __align__(8) uint64_t sfree[kPairSlots];     // this CTA's writers done with the slot
   __shared__ __align__(8) uint64_t full[kPairSlots];      // leader: both CTAs' scales written
-  __shared__ __align__(8) uint64_t sempty[kPairSlots];    // pair MMAs done with the scale slot
+  __shared__ __align__(8) uint64_t tfree[kPairSlots];     // pair MMAs done with the tensor-memory slot
   __shared__ __align__(8) uint64_t acc_full;
   __shared__ __align__(8) uint64_t acc_empty;             // leader: both epilogues drained
   __shared__ __align__(8) uint64_t drained;               // leader: every issued MMA finished
@@ -213,8 +215,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
     for (int s = 0; s < kPairSlots; ++s) {
       mbar_init(&sloaded[s], 1);
+      mbar_init(&sfree[s], kPairScaleWarps);
       mbar_init(&full[s], 2 * kPairScaleWarps);
-      mbar_init(&sempty[s], 1);
+      mbar_init(&tfree[s], 1);
     }
     mbar_init(&acc_full, 1);
     mbar_init(&acc_empty, 2 * kPairEpiWarps);
@@ -312,7 +315,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
           }
           tc_commit_pair(&empty[s], 0x3);
-          tc_commit_pair(&sempty[slot], 0x3);
+          tc_commit_pair(&tfree[slot], 0x3);
         }
         if (abort_flag) break;
         tc_commit_pair(&acc_full, 0x3);
@@ -418,10 +421,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     int sb = 0;  // stage block of `it` within its tile
     for (int it = 0; it < my_stages; ++it) {
       const int slot = it % kPairSlots;
-      // Warp-uniform exit: tcgen05.st needs the whole warp.
-      if (!__all_sync(0xffffffffu, pair_wait(&sloaded[slot],
-                                             static_cast<uint32_t>(it / kPairSlots) & 1u,
-                                             kPairIdleSleepNs)))
+      // Warp-uniform exit: tcgen05.st needs the whole warp.  The stage's
+      // scales have landed, and the MMAs that read the tensor-memory slot's
+      // previous contents (kPairSlots stages back) have finished.
+      const uint32_t round = static_cast<uint32_t>(it / kPairSlots) & 1u;
+      if (!__all_sync(0xffffffffu, pair_wait(&sloaded[slot], round, kPairIdleSleepNs) &&
+                                       pair_wait(&tfree[slot], round ^ 1u, kPairIdleSleepNs)))
         break;
       const int nkb = min(kPairPanels, args.kblocks - sb * kPairPanels);
       if (++sb == stage_blocks) sb = 0;
@@ -439,21 +444,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&full[slot]), 0));
+      if (lane == 0) {
+        mbar_arrive(&sfree[slot]);  // the shared-memory slot may be refilled
+        mbar_arrive_cluster(mapa_shared(smem_addr(&full[slot]), 0));
+      }
     }
   } else if (lane == 0) {
     // -------------------------------------------------------- scale loader
-    // Scales of each stage into slot j % kPairSlots as soon as the slot's
-    // previous stage has been consumed: [A own rows][B rows 0-127][B rows
-    // 128-255], nkb KiB each (consecutive K blocks of a row block are
-    // contiguous in the packed layout).  Its own warp, so neither the operand
-    // producer nor the scale writers wait for these copies to be issued.
+    // Scales of each stage into slot j % kPairSlots as soon as this CTA's
+    // writers have moved the slot's previous stage into tensor memory (not
+    // when its MMAs finish, which would leave the loads only about three
+    // stages of lead): [A own rows][B rows 0-127][B rows 128-255], nkb KiB
+    // each (consecutive K blocks of a row block are contiguous in the packed
+    // layout).  Its own warp, so neither the operand producer nor the scale
+    // writers wait for these copies to be issued.
     const size_t rb_bytes = static_cast<size_t>(args.kblocks) * 1024;
     PairCursor sc;
     sc.start(pair, args);
     for (int j = 0; j < my_stages && !abort_flag; ++j) {
       const int slot = j % kPairSlots;
-      if (!pair_wait(&sempty[slot], (static_cast<uint32_t>(j / kPairSlots) & 1u) ^ 1u)) break;
+      if (!pair_wait(&sfree[slot], (static_cast<uint32_t>(j / kPairSlots) & 1u) ^ 1u)) break;
       uint8_t* ss = smem + kPairSlotOffset + slot * kPairSlotBytes;
       const uint32_t sbytes = static_cast<uint32_t>(sc.nkb) * 1024;
       mbar_arrive_expect_tx(&sloaded[slot], 3 * sbytes);
