@@ -74,14 +74,16 @@ def test_copy_matches_oracle_copy(cuda, native):
 
 @pytest.mark.parametrize("dtype,code", [(torch.float32, 0), (torch.float16, 1),
                                         (torch.bfloat16, 2)])
-@pytest.mark.parametrize("block", [1024, 16384])
-def test_read_block_sums(cuda, native, dtype, code, block):
+@pytest.mark.parametrize("block,threads", [(1024, 256), (16384, 256), (16384, 1024)])
+def test_read_block_sums(cuda, native, dtype, code, block, threads):
+    """Whole blocks of 1-8 vectors per thread take the batched loads, others
+    (and the partial last block) the loop; both against the oracle."""
     n = 3 * block * 7 + 17  # partial last block
     gen = torch.Generator().manual_seed(block)
     host = torch.randn(n, generator=gen).to(dtype)
     src = host.to(cuda)
     sink = torch.full((-(-n // block),), float("nan"), device=cuda)
-    native.read(src, code, n, sink, block, 256)
+    native.read(src, code, n, sink, block, threads)
     torch.cuda.synchronize()
     sums, abs_sums = oracle_native.block_sums(host.float().numpy(), block)
     tol = abs_sums * 2 * np.finfo(np.float32).eps * max(1, np.log2(block)) + 1e-6
