@@ -146,3 +146,13 @@ def test_entry_points_reject_bad_arguments_before_touching_a_device(native):
     assert lib.tcb_tensor_peak(native.T_FP64, native.TV_DMMA, fake, fake, None, None, fake, 0, 1,
                                128, 128, 16, 1, 1, None, None) == native.ERR_INVALID_ARGUMENT
     assert lib.tcb_kernel_info(99, 0, 0, 0, 0, 0, 0, 0, None) == native.ERR_INVALID_ARGUMENT
+
+
+def test_vector_coefficient_source_per_op(native):
+    """Packed bf16/fp16 and DP4A chains take device coefficients (registers);
+    the other ops take the host copy (passed by value, constant bank)."""
+    on_device, on_host = object(), object()
+    for code in (native.V_BF16, native.V_FP16, native.V_INT8_DP4A):
+        assert native.vector_coefficients(code, on_device, on_host) is on_device
+    for code in (native.V_FP32, native.V_FP64, native.V_INT32_IMAD, native.V_INT8_MULADD):
+        assert native.vector_coefficients(code, on_device, on_host) is on_host
