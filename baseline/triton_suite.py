@@ -104,7 +104,7 @@ def main() -> int:
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--install", type=Path, metavar="REFERENCE",
                         help="copy the reference suite's modules into baseline/_ref and exit")
-    parser.add_argument("--output", type=Path, default=Path("gpurun_out/triton_suite.json"))
+    parser.add_argument("--output", type=Path, default=Path("triton_suite.json"))
     parser.add_argument("--compare", type=Path, metavar="OURS",
                         help="print this repository's table JSON beside the reference's")
     parser.add_argument("--summary", type=Path, nargs=2, metavar=("SUITE_JSON", "OUT"),
